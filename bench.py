@@ -1,0 +1,423 @@
+"""Benchmark: paged decode attention HBM GB/s (and decode tokens/s) on B200.
+
+Default workload (N=1): INT8 paged decode attention at the GPT-2-small shape,
+batch 32, 12 heads (MHA), head_dim 64, block_size 16, every context ~1024,
+fp16 K/V/Q ~ N(0,1), physical pages shuffled by the allocator.  One step is a
+decode step over 12 layers (GPT-2 small depth, one pool per layer): one
+allocator/planner launch, then per layer the KV append of one new token per
+sequence (a page commit every 16 steps) and the fused attention.  The 12
+pools (~610 MB) exceed the 126 MB L2, so no flush is needed between steps.
+
+Contexts start at 1024 - W - 1 so the K timed steps run at 1024 .. 1024+K-1.
+
+Metric value = algorithmic HBM bytes of the step (codes, scales, block table,
+staged tail, q, out, append traffic; each byte counted once) / device time.
+With --gpus N (torchrun) every rank runs the same per-GPU workload on its own
+sequences (weak scaling) and the last layer's outputs are gathered with NCCL
+all_gather once per step; time is the max over ranks.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload gpt2_int8|tinyllama_int4]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    # config: INT8 MHA, GPT-2 small
+    "gpt2_int8": dict(batch=32, hq=12, hkv=12, d=64, page=16, ctx=1024, layers=12, kv="int8",
+                      desc="INT8 paged decode attention, GPT-2-small shape: batch 32, 12 heads, head_dim 64, "
+                           "block 16, context 1024, 12 layers, 1 new token/seq/step"),
+    # config: INT4 GQA, TinyLlama attention shape, contexts U[128, 2048], 1% outliers x8
+    "tinyllama_int4": dict(batch=64, hq=32, hkv=4, d=64, page=16, ctx="uniform128_2048", layers=22, kv="int4",
+                           desc="INT4 paged decode attention with GQA (32q/4kv), head_dim 64, block 16, batch 64, "
+                                "contexts U[128,2048], 22 layers, 1% outliers x8"),
+}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# --------------------------------------------------------------------------
+# algorithmic bytes (counted once per byte that must move)
+# --------------------------------------------------------------------------
+
+def attention_bytes(lens, w):
+    """Bytes one attention launch must touch: committed codes K+V, per-page scales
+    K+V, block-table entries, staged fp16 tail K+V, q and out (fp16)."""
+    bq = 1.0 if w["kv"] == "int8" else 0.5
+    P, hkv, d, hq = w["page"], w["hkv"], w["d"], w["hq"]
+    tot = 0.0
+    for c in lens:
+        n, r = c // P, c % P
+        tot += 2 * n * P * hkv * d * bq + 2 * 4 * n + 4 * n + 2 * 2 * r * hkv * d + 2 * 2 * hq * d
+    return tot
+
+
+def append_bytes(lens_after, w):
+    """One new token per sequence: read it (K+V fp16); a filling page also reads
+    its P-1 staged rows and writes P rows of codes + 2 scales, otherwise the
+    token is written to staging."""
+    bq = 1.0 if w["kv"] == "int8" else 0.5
+    P, hkv, d = w["page"], w["hkv"], w["d"]
+    row = hkv * d
+    tot = 0.0
+    for c in lens_after:
+        tot += 2 * row * 2
+        if c % P == 0:
+            tot += 2 * (P - 1) * row * 2 + 2 * P * row * bq + 8
+        else:
+            tot += 2 * row * 2
+    return tot
+
+
+# --------------------------------------------------------------------------
+# clocks sampling during the timed region
+# --------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------
+# workload construction
+# --------------------------------------------------------------------------
+
+def contexts_for(w, batch, seed, start_offset):
+    g = torch.Generator().manual_seed(seed)
+    if w["ctx"] == "uniform128_2048":
+        c = torch.randint(128, 2049, (batch,), generator=g)
+    else:
+        c = torch.full((batch,), int(w["ctx"]))
+    return (c - start_offset).clamp(min=1).to(torch.int32)
+
+
+def build(w, warmup, steps, device, seed):
+    from metagross_b200.batched import BatchedPagedKVCache
+
+    B, L, hkv, d, P, hq = w["batch"], w["layers"], w["hkv"], w["d"], w["page"], w["hq"]
+    start = contexts_for(w, B, seed, warmup + 1)
+    max_final = int(start.max()) + warmup + steps + 1
+    max_blocks = max_final // P + 2
+    # pool with slack so physical pages come out of a shuffled free list
+    num_pages = B * max_blocks + 256
+    cache = BatchedPagedKVCache(L, B, hkv, d, page_size=P, num_pages=num_pages, max_blocks=max_blocks,
+                                kv_dtype=w["kv"], staging_dtype=torch.float16, device=device)
+    cache._workspace(hq, max_final)  # size the split workspace once, outside any timed region
+    # shuffle the allocator's free stack so logical pages land on random physical pages
+    g = torch.Generator().manual_seed(seed + 1)
+    perm = torch.randperm(num_pages, generator=g).to(torch.int32)
+    cache.allocator.free_stack.copy_(perm.to(device))
+    gd = torch.Generator(device=device).manual_seed(seed + 2)
+    # prefill every layer to the start contexts
+    cache.begin_step(start)
+    T = int(start.max())
+    for layer in range(L):
+        k = torch.randn(B, T, hkv, d, generator=gd, device=device, dtype=torch.float16)
+        v = torch.randn(B, T, hkv, d, generator=gd, device=device, dtype=torch.float16)
+        if w["kv"] == "int4":  # 1% outliers x8
+            k[torch.rand(k.shape, generator=gd, device=device) < 0.01] *= 8
+            v[torch.rand(v.shape, generator=gd, device=device) < 0.01] *= 8
+        cache.append(layer, k, v)
+        del k, v
+    torch.cuda.synchronize()
+    cache.check()
+    # per-step inputs (device), distinct per layer
+    q = torch.randn(L, B, hq, d, generator=gd, device=device, dtype=torch.float16)
+    kn = torch.randn(L, B, 1, hkv, d, generator=gd, device=device, dtype=torch.float16)
+    vn = torch.randn(L, B, 1, hkv, d, generator=gd, device=device, dtype=torch.float16)
+    out = torch.empty(L, B, hq, d, device=device, dtype=torch.float16)
+    return cache, start, q, kn, vn, out
+
+
+def run_step(cache, q, kn, vn, out, ev=None):
+    """One decode step over all layers; ev: list of (start, end) event pairs around each attention."""
+    cache.begin_step(1)
+    for layer in range(cache.num_layers):
+        cache.append(layer, kn[layer], vn[layer])
+        if ev is not None:
+            ev[layer][0].record()
+        cache.attend(layer, q[layer], out=out[layer], max_context=cache._max_len)
+        if ev is not None:
+            ev[layer][1].record()
+
+
+# --------------------------------------------------------------------------
+# CPU path (the reference's CPU implementation, restated in the oracle)
+# --------------------------------------------------------------------------
+
+def cpu_sample_gbs(w, seconds=10.0, seed=0):
+    """Time the oracle's fp32 numpy CPU path (dequantize pages, then attend --
+    the reference's tests/reference.py + torch-CPU path) on whole sequences of
+    the same workload until ~``seconds`` pass.  Returns (GB/s, cores, sample)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle_cpu
+
+    return oracle_cpu.time_decode_sample(w, seconds=seconds, seed=seed)
+
+
+# --------------------------------------------------------------------------
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def traffic_per_launch(workload):
+    """dram bytes per attention launch from the committed ncu summary, if present."""
+    p = os.path.join(ROOT, "profiles", f"decode_attention_{workload}.txt")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="gpt2_int8")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    w = WORKLOADS[args.workload]
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    metric = "paged decode attn HBM GB/s"
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        gbs, cores, sample = cpu_sample_gbs(w, seconds=max(1.0, min(args.cpu_seconds, 30.0)))
+        line = {"impl": "reference", "metric": metric, "value": gbs, "unit": "GB/s", "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": args.workload, "desc": w["desc"]},
+                "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample},
+                "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+
+    cache, start, q, kn, vn, out = build(w, args.warmup, args.steps, device, seed=1234 + rank)
+    L, B = w["layers"], w["batch"]
+    gather_buf = None
+    if world > 1:
+        gather_buf = torch.empty(world * B, w["hq"], w["d"], device=device, dtype=torch.float16)
+
+    def step(ev=None):
+        run_step(cache, q, kn, vn, out, ev)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.all_gather_into_tensor(gather_buf, out[L - 1])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    cache.check()
+
+    # bytes of the timed steps (contexts known on the host)
+    lens0 = start + args.warmup  # lengths before the first timed step
+    att_b, app_b = 0.0, 0.0
+    for s in range(args.steps):
+        after = (lens0 + s + 1).tolist()
+        att_b += L * attention_bytes(after, w)
+        app_b += L * append_bytes(after, w)
+    step_bytes = (att_b + app_b) / args.steps
+    att_bytes_per_launch = att_b / (args.steps * L)
+
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
+          for _ in range(args.steps)]
+    clocks = ClockSampler(local)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for s in range(args.steps):
+        step(ev[s])
+    t1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1)
+    att_ms = [ev[s][l][0].elapsed_time(ev[s][l][1]) for s in range(args.steps) for l in range(L)]
+    att_avg_ms = sum(att_ms) / len(att_ms)
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([ms, att_avg_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, att_avg_ms = float(t[0]), float(t[1])
+    cache.check()
+
+    # ---- end to end through the public API with host buffers -----------------
+    e2e = None
+    if True:
+        qh = q.cpu().pin_memory()
+        knh, vnh = kn.cpu().pin_memory(), vn.cpu().pin_memory()
+        outh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        qd, knd, vnd = torch.empty_like(q), torch.empty_like(kn), torch.empty_like(vn)
+        e2e_steps = max(3, args.steps // 2)
+        lens_e = (lens0 + args.steps).clone()
+        e_bytes = 0.0
+        for s in range(e2e_steps):
+            after = (lens_e + s + 1).tolist()
+            e_bytes += L * (attention_bytes(after, w) + append_bytes(after, w))
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for s in range(e2e_steps):
+            qd.copy_(qh, non_blocking=True)
+            knd.copy_(knh, non_blocking=True)
+            vnd.copy_(vnh, non_blocking=True)
+            run_step(cache, qd, knd, vnd, out)
+            if world > 1:
+                import torch.distributed as dist
+
+                dist.all_gather_into_tensor(gather_buf, out[L - 1])
+            outh.copy_(out, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        e_ms = e0.elapsed_time(e1)
+        if world > 1:
+            import torch.distributed as dist
+
+            t = torch.tensor([e_ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = float(t[0])
+        e2e = {"value": world * e_bytes / (e_ms / 1e3) / 1e9, "unit": "GB/s",
+               "h2d_bytes_per_step": int(q.numel() * 2 + kn.numel() * 2 + vn.numel() * 2),
+               "d2h_bytes_per_step": int(out.numel() * 2),
+               "ms_per_step": e_ms / e2e_steps}
+        cache.check()
+
+    if rank == 0:
+        peak, peak_kind = peaks()
+        achieved = att_bytes_per_launch / (att_avg_ms / 1e3) / 1e9
+        value = world * step_bytes / (ms / args.steps / 1e3) / 1e9
+        tok_s = world * B * args.steps / (ms / 1e3)
+        line = {
+            "metric": metric, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": w["kv"] if w["kv"] == "int8" else "int4", "data": "synthetic",
+            "config": {"workload": args.workload, "desc": w["desc"], "global_batch": world * B,
+                       "context_mean": float((lens0 + (args.steps + 1) / 2).float().mean()),
+                       "layers": L, "parallelism": f"sequence-sharded dp{world}",
+                       "l2": "working set per step > 126 MB L2 (one pool per layer); no flush"},
+            "decode_tokens_per_s": round(tok_s, 1),
+            "bytes_per_step": step_bytes * world,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "traffic": traffic_per_launch(args.workload),
+                         "kernel": "paged_decode_kernel", "algorithmic_bytes_per_launch": att_bytes_per_launch,
+                         "avg_launch_ms": att_avg_ms},
+            "e2e": e2e,
+            "gpu_launches": args.steps * (1 + 2 * L),
+            "clocks": clk,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            gbs, cores, sample = cpu_sample_gbs(w, seconds=args.cpu_seconds)
+            line["cpu_baseline"] = {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample}
+        print(json.dumps(line), flush=True)
+
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

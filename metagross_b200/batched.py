@@ -1,0 +1,191 @@
+"""Batched, device-resident paged KV cache and decode attention.
+
+This is the fast path behind the reference's per-sequence API: the same page
+layout, scale layout, commit rule and allocator order as metagross/cache.py
+and metagross/allocator.py, but for a batch of sequences and all layers, with
+every piece of state in device memory and no host synchronisation per step.
+
+State (per cache):
+  k_pool, v_pool   [L, N, P, Hkv, D] int8  or [L, N, P, Hkv, D/2] uint8 (INT4)
+  k_scales, v_scales [L, N] fp32, one scale per physical page
+  staging_k/v      [L, B, P, Hkv, D] (fp16 or fp32): the page being filled,
+                   exact, never quantized
+  block_tables     [B, max_blocks] int32, shared by all layers (every layer
+                   commits at the same token counts, so one table serves all)
+  seq_lens         [B] int32 tokens cached per sequence
+  allocator        DeviceBlockAllocator (LIFO, reference order)
+  status           [1] int32 error bits set by kernels (see MG_DEV_* in
+                   include/metagross_b200.h); ``check()`` reads it
+
+A decode/prefill step is:
+  cache.begin_step(n_new)              # allocate committing pages (once)
+  for layer: cache.append(layer, k, v) # quantize filled pages, stage the rest
+             out = cache.attend(layer, q)
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .allocator import DeviceBlockAllocator
+
+MG_DEV_BITS = {
+    0x1: "out of pages",
+    0x2: "block-table id out of range",
+    0x4: "double free",
+    0x8: "bulk-copy wait timed out",
+    0x10: "block-table row full",
+    0x20: "work skipped after an earlier error",
+    0x40: "sequence longer than max_context",
+    0x80: "inconsistent per-sequence argument",
+}
+
+
+def _get_C():
+    from . import _C
+
+    return _C
+
+
+class BatchedPagedKVCache:
+    def __init__(self, num_layers, batch, num_kv_heads, head_dim, page_size=16, num_pages=None, max_blocks=None,
+                 kv_dtype="int8", staging_dtype=torch.float16, device="cuda"):
+        if kv_dtype not in ("int8", "int4"):
+            raise ValueError(f"kv_dtype must be 'int8' or 'int4', got {kv_dtype!r}")
+        for name, v in (("num_layers", num_layers), ("batch", batch), ("num_kv_heads", num_kv_heads),
+                        ("head_dim", head_dim), ("page_size", page_size)):
+            if v <= 0:
+                raise ValueError(f"{name} must be positive, got {v}")
+        if kv_dtype == "int4" and head_dim % 32:
+            raise ValueError("INT4 pools need head_dim % 32 == 0")
+        if staging_dtype not in (torch.float16, torch.float32):
+            raise ValueError("staging_dtype must be torch.float16 or torch.float32")
+        self.num_layers, self.batch = num_layers, batch
+        self.num_kv_heads, self.head_dim, self.page_size = num_kv_heads, head_dim, page_size
+        self.kv_dtype = kv_dtype
+        self.staging_dtype = staging_dtype
+        self.device = torch.device(device)
+        self.max_blocks = int(max_blocks) if max_blocks else 64
+        self.num_pages = int(num_pages) if num_pages else batch * self.max_blocks
+        row = head_dim if kv_dtype == "int8" else head_dim // 2
+        dt = torch.int8 if kv_dtype == "int8" else torch.uint8
+        shape = (num_layers, self.num_pages, page_size, num_kv_heads, row)
+        self.k_pool = torch.zeros(shape, dtype=dt, device=self.device)
+        self.v_pool = torch.zeros(shape, dtype=dt, device=self.device)
+        self.k_scales = torch.zeros(num_layers, self.num_pages, dtype=torch.float32, device=self.device)
+        self.v_scales = torch.zeros_like(self.k_scales)
+        st = (num_layers, batch, page_size, num_kv_heads, head_dim)
+        self.staging_k = torch.zeros(st, dtype=staging_dtype, device=self.device)
+        self.staging_v = torch.zeros(st, dtype=staging_dtype, device=self.device)
+        self.block_tables = torch.zeros(batch, self.max_blocks, dtype=torch.int32, device=self.device)
+        self.seq_lens = torch.zeros(batch, dtype=torch.int32, device=self.device)
+        self.n_new = torch.zeros(batch, dtype=torch.int32, device=self.device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.allocator = DeviceBlockAllocator(self.num_pages, self.device)
+        self._max_len = 0  # host-side upper bound on seq_lens
+        self._ws = torch.zeros(0, dtype=torch.uint8, device=self.device)
+        self._ws_key = None
+
+    # ------------------------------------------------------------------ steps
+    def begin_step(self, n_new) -> None:
+        """Grow every sequence by n_new tokens (int or int32 tensor [B]); allocate the pages that fill."""
+        C = _get_C()
+        if isinstance(n_new, int):
+            if n_new < 0:
+                raise ValueError("n_new must be >= 0")
+            self.n_new.fill_(n_new)
+            self._max_len += n_new
+        else:
+            t = torch.as_tensor(n_new, dtype=torch.int32)
+            if t.device.type == "cpu":
+                self._max_len += int(t.max()) if t.numel() else 0
+            else:
+                self._max_len = self.max_blocks * self.page_size + self.page_size - 1
+            self.n_new.copy_(t.to(self.device), non_blocking=True)
+        self._max_len = min(self._max_len, self.max_blocks * self.page_size + self.page_size - 1)
+        C.plan_append(self.allocator.free_stack, self.allocator.n_free, self.allocator.in_use, self.block_tables,
+                      self.seq_lens, self.n_new, self.page_size, self.status)
+
+    def append(self, layer: int, k_new: torch.Tensor, v_new: torch.Tensor) -> None:
+        """Write this step's tokens of one layer: k_new/v_new [B, T, Hkv, D] (fp16/fp32), n_new[b] <= T used."""
+        if k_new.dim() == 3:
+            k_new, v_new = k_new.unsqueeze(1), v_new.unsqueeze(1)
+        _get_C().kv_append(self.k_pool[layer], self.v_pool[layer], self.k_scales[layer], self.v_scales[layer],
+                           self.staging_k[layer], self.staging_v[layer], self.block_tables, self.seq_lens,
+                           self.n_new, k_new, v_new, self.status)
+
+    def _workspace(self, num_q_heads: int, max_context: int) -> torch.Tensor:
+        key = (num_q_heads, max_context)
+        if key != self._ws_key:
+            nbytes = _get_C().decode_workspace_bytes(self.k_pool[0], self.block_tables, num_q_heads, max_context)
+            if nbytes > self._ws.numel():
+                self._ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+            self._ws_key = key
+        return self._ws
+
+    def attend(self, layer: int, q: torch.Tensor, scale: float | None = None, out: torch.Tensor | None = None,
+               max_context: int | None = None) -> torch.Tensor:
+        """softmax(scale q K^T) V over committed pages + staged tail; q [B, Hq, D] fp16/fp32."""
+        if q.dim() != 3 or q.shape[0] != self.batch or q.shape[2] != self.head_dim:
+            raise ValueError(f"q must be [{self.batch}, num_q_heads, {self.head_dim}], got {tuple(q.shape)}")
+        hq = q.shape[1]
+        if hq % self.num_kv_heads:
+            raise ValueError(f"num_q_heads={hq} must be divisible by num_kv_heads={self.num_kv_heads}")
+        sc = 1.0 / math.sqrt(self.head_dim) if scale is None else float(scale)
+        if not (sc > 0 and math.isfinite(sc)):
+            raise ValueError(f"scale must be a positive finite number, got {scale}")
+        mc = int(max_context) if max_context else max(self._max_len, 1)
+        ws = self._workspace(hq, mc)
+        if out is None:
+            out = torch.empty_like(q)
+        _get_C().paged_decode_attention(q.contiguous(), self.k_pool[layer], self.v_pool[layer], self.k_scales[layer],
+                                        self.v_scales[layer], self.staging_k[layer], self.staging_v[layer],
+                                        self.block_tables, self.seq_lens, sc, mc, ws, out, self.status)
+        return out
+
+    def gather(self, layer: int, dtype=torch.float32, include_staging: bool = True):
+        """Dequantized K, V of every sequence, packed: ([total, Hkv, D], [total, Hkv, D], cu_seqlens [B+1])."""
+        lens = self.seq_lens.to("cpu")
+        if not include_staging:
+            lens = (lens // self.page_size) * self.page_size
+        cu = torch.zeros(self.batch + 1, dtype=torch.int32)
+        cu[1:] = torch.cumsum(lens, 0)
+        total = int(cu[-1])
+        ok = torch.empty(total, self.num_kv_heads, self.head_dim, dtype=dtype, device=self.device)
+        ov = torch.empty_like(ok)
+        mc = max(int(lens.max()) if lens.numel() else 0, 1)
+        _get_C().gather_dequant(self.k_pool[layer], self.v_pool[layer], self.k_scales[layer], self.v_scales[layer],
+                                self.staging_k[layer] if include_staging else None,
+                                self.staging_v[layer] if include_staging else None, self.block_tables,
+                                self.seq_lens, cu.to(self.device), mc, ok, ov, self.status)
+        return ok, ov, cu
+
+    def free(self, seq_ids) -> None:
+        """Return every page of the given sequences to the pool and reset them to length 0."""
+        ids = torch.as_tensor(seq_ids, dtype=torch.int32).to(self.device)
+        _get_C().free_sequences(self.allocator.free_stack, self.allocator.n_free, self.allocator.in_use,
+                                self.block_tables, self.seq_lens, ids, self.page_size, self.status)
+
+    def reset(self) -> None:
+        self.allocator.reset()
+        self.seq_lens.zero_()
+        self.block_tables.zero_()
+        self.status.zero_()
+        self._max_len = 0
+
+    # ------------------------------------------------------------- inspection
+    def check(self) -> None:
+        """Raise RuntimeError if a kernel reported an error (synchronises)."""
+        s = int(self.status.item())
+        if s:
+            names = [v for k, v in MG_DEV_BITS.items() if s & k]
+            raise RuntimeError(f"paged KV cache device error 0x{s:x}: {', '.join(names)}")
+
+    def memory_bytes(self) -> int:
+        return self.k_pool.numel() + self.v_pool.numel()
+
+
+def paged_decode_attention(cache: BatchedPagedKVCache, layer: int, q: torch.Tensor, scale=None, out=None):
+    """Functional form of ``BatchedPagedKVCache.attend``."""
+    return cache.attend(layer, q, scale=scale, out=out)

@@ -1,0 +1,538 @@
+// Device-resident paged cache: page allocator, step planner, KV append with
+// page commit (quantize), block gather/dequantize, sequence free.
+//
+// Semantics are those of the reference's per-sequence Python cache
+// (metagross/cache.py:45-85) and allocator (metagross/allocator.py:1-33),
+// batched: one pool and one LIFO allocator serve every sequence of the batch
+// and every layer (all layers commit at the same token counts, so one block
+// table per sequence serves them all -- the reference's 2*num_layers
+// allocators of one sequence all hand out the same ids).
+#include "mg_common.cuh"
+
+namespace mg {
+namespace {
+
+constexpr int kPlanThreads = 1024;
+constexpr int kAppendThreads = 256;
+constexpr int kGatherThreads = 256;
+
+// Block-wide exclusive scan of one int per thread; returns the exclusive
+// prefix, *total receives the block sum.  scratch >= 33 ints.
+__device__ int block_exclusive_scan(int v, int* scratch, int* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nw = (blockDim.x + 31) >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    __syncthreads();
+    if (lane == 31) scratch[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < nw ? scratch[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            int y = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += y;
+        }
+        if (lane < nw) scratch[lane] = w;  // inclusive per-warp offsets
+        if (lane == nw - 1) scratch[32] = w;
+    }
+    __syncthreads();
+    const int warp_off = warp == 0 ? 0 : scratch[warp - 1];
+    *total = scratch[32];
+    return warp_off + x - v;
+}
+
+__global__ void alloc_init_kernel(int32_t* free_stack, int32_t* n_free, int32_t* in_use, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        free_stack[i] = static_cast<int32_t>(i);
+        in_use[i] = 0;
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) *n_free = static_cast<int32_t>(n);
+}
+
+constexpr int32_t kStopBits = MG_DEV_OUT_OF_PAGES | MG_DEV_BLOCK_TABLE_FULL;
+
+// One CTA.  Pass 1 validates the whole step, pass 2 applies it, so a failed
+// step changes nothing.
+__global__ void __launch_bounds__(kPlanThreads) plan_append_kernel(int32_t* free_stack, int32_t* n_free_p,
+                                                                   int32_t* in_use, int32_t* block_tables,
+                                                                   int32_t max_blocks, int32_t* seq_lens,
+                                                                   const int32_t* n_new, int32_t batch,
+                                                                   int32_t P, int32_t* status) {
+    __shared__ int scratch[33];
+    __shared__ int s_flags;
+    if (threadIdx.x == 0) s_flags = 0;
+    __syncthreads();
+    if (status && (*(volatile int32_t*)status & kStopBits)) {
+        if (threadIdx.x == 0) flag(status, MG_DEV_SKIPPED);
+        return;
+    }
+    int local = 0;
+    int bad = 0;
+    for (int b = threadIdx.x; b < batch; b += blockDim.x) {
+        const int old = seq_lens[b], add = n_new[b];
+        if (add < 0 || old < 0) { bad = 1; continue; }
+        const int nw = old + add;
+        if (nw / P > max_blocks) bad = 1;
+        local += nw / P - old / P;
+    }
+    int total;
+    if (bad) atomicOr(&s_flags, 1);
+    (void)block_exclusive_scan(local, scratch, &total);
+    __syncthreads();
+    const int n_free = *n_free_p;
+    if (s_flags) {
+        if (threadIdx.x == 0) flag(status, MG_DEV_BLOCK_TABLE_FULL);
+        return;
+    }
+    if (total > n_free) {
+        if (threadIdx.x == 0) flag(status, MG_DEV_OUT_OF_PAGES);
+        return;
+    }
+    int base = 0;
+    for (int start = 0; start < batch; start += blockDim.x) {
+        const int b = start + threadIdx.x;
+        int old = 0, nw = 0, c = 0;
+        if (b < batch) {
+            old = seq_lens[b];
+            nw = old + n_new[b];
+            c = nw / P - old / P;
+        }
+        int chunk_total;
+        const int excl = block_exclusive_scan(c, scratch, &chunk_total) + base;
+        if (b < batch) {
+            int32_t* row = block_tables + static_cast<int64_t>(b) * max_blocks;
+            for (int j = 0; j < c; ++j) {
+                const int32_t page = free_stack[n_free - 1 - (excl + j)];
+                row[old / P + j] = page;
+                in_use[page] = 1;
+            }
+            seq_lens[b] = nw;
+        }
+        base += chunk_total;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) *n_free_p = n_free - total;
+}
+
+// Frees the listed sequences' pages in (list order, block-table order).
+__global__ void __launch_bounds__(kPlanThreads) free_sequences_kernel(int32_t* free_stack, int32_t* n_free_p,
+                                                                      int32_t* in_use, int64_t num_pages,
+                                                                      const int32_t* block_tables,
+                                                                      int32_t max_blocks, int32_t* seq_lens,
+                                                                      int32_t batch, const int32_t* seq_ids,
+                                                                      int32_t num_seqs, int32_t P, int32_t* status) {
+    __shared__ int scratch[33];
+    int top = *n_free_p;
+    for (int i = 0; i < num_seqs; ++i) {
+        const int s = seq_ids[i];
+        if (s < 0 || s >= batch) {
+            if (threadIdx.x == 0) flag(status, MG_DEV_BAD_ARGUMENT);
+            continue;
+        }
+        int npages = seq_lens[s] / P;
+        if (npages > max_blocks) npages = max_blocks;
+        const int32_t* row = block_tables + static_cast<int64_t>(s) * max_blocks;
+        for (int start = 0; start < npages; start += blockDim.x) {
+            const int j = start + threadIdx.x;
+            int ok = 0;
+            int32_t page = -1;
+            if (j < npages) {
+                page = row[j];
+                if (page < 0 || page >= num_pages) {
+                    flag(status, MG_DEV_BAD_PAGE_ID);
+                } else if (atomicExch(&in_use[page], 0) != 1) {
+                    flag(status, MG_DEV_DOUBLE_FREE);
+                } else {
+                    ok = 1;
+                }
+            }
+            int cnt;
+            const int excl = block_exclusive_scan(ok, scratch, &cnt);
+            if (ok) free_stack[top + excl] = page;
+            top += cnt;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) seq_lens[s] = 0;
+    }
+    if (threadIdx.x == 0) *n_free_p = top;
+}
+
+// ---------------------------------------------------------------------------
+// KV append: one CTA per (sequence, touched page, K|V).
+// ---------------------------------------------------------------------------
+template <typename T>
+struct Vec8;  // 8 consecutive elements
+template <>
+struct Vec8<float> {
+    static __device__ __forceinline__ void load(const float* p, float (&v)[8]) {
+        const float4 a = *reinterpret_cast<const float4*>(p);
+        const float4 b = *reinterpret_cast<const float4*>(p + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    }
+    static __device__ __forceinline__ void store(float* p, const float (&v)[8]) {
+        *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+    }
+};
+template <>
+struct Vec8<__half> {
+    static __device__ __forceinline__ void load(const __half* p, float (&v)[8]) {
+        const uint4 u = *reinterpret_cast<const uint4*>(p);
+        const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(h[i]);
+            v[2 * i] = f.x;
+            v[2 * i + 1] = f.y;
+        }
+    }
+    static __device__ __forceinline__ void store(__half* p, const float (&v)[8]) {
+        uint4 u;
+        __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+        *reinterpret_cast<uint4*>(p) = u;
+    }
+};
+
+struct AppendParams {
+    const void* k_new;
+    const void* v_new;
+    int32_t max_new;
+    void* k_pool;
+    void* v_pool;
+    float* k_scales;
+    float* v_scales;
+    void* staging_k;
+    void* staging_v;
+    const int32_t* block_tables;
+    int32_t max_blocks;
+    const int32_t* seq_lens;
+    const int32_t* n_new;
+    int32_t P;
+    int32_t row;  // Hkv * D elements per token
+    int64_t num_pages;
+    int32_t* status;
+};
+
+template <bool INT4, typename ST, typename NT>
+__global__ void __launch_bounds__(kAppendThreads) kv_append_kernel(AppendParams p) {
+    __shared__ float red[32];
+    const int b = blockIdx.x, jj = blockIdx.y, kv = blockIdx.z;
+    if (p.status && (*(volatile int32_t*)p.status & kStopBits)) return;
+    const int new_len = p.seq_lens[b], add = p.n_new[b];
+    if (add <= 0) return;
+    if (add > p.max_new || add > new_len) {
+        if (jj == 0 && kv == 0 && threadIdx.x == 0) flag(p.status, MG_DEV_BAD_ARGUMENT);
+        return;
+    }
+    const int old = new_len - add;
+    const int P = p.P, row = p.row;
+    const int j0 = old / P, jlast = (new_len - 1) / P;
+    const int j = j0 + jj;
+    if (j > jlast) return;
+    const int64_t pe = static_cast<int64_t>(P) * row;  // elements per page
+    ST* staging = static_cast<ST*>(kv ? p.staging_v : p.staging_k) + static_cast<int64_t>(b) * pe;
+    const NT* src_new = static_cast<const NT*>(kv ? p.v_new : p.k_new) + static_cast<int64_t>(b) * p.max_new * row;
+    const int page_start = j * P;
+
+    if (page_start + P <= new_len) {  // page j fills during this step: commit it
+        const int32_t page = j < p.max_blocks ? p.block_tables[static_cast<int64_t>(b) * p.max_blocks + j] : -1;
+        if (page < 0 || page >= p.num_pages) {
+            if (threadIdx.x == 0) flag(p.status, MG_DEV_BAD_PAGE_ID);
+        } else {
+            // element e of the page: token t = e / row
+            float a = 0.0f;
+            for (int64_t e = threadIdx.x * 8; e < pe; e += kAppendThreads * 8) {
+                const int t = static_cast<int>(e / row);
+                const int tok = page_start + t;
+                const int64_t c = e - static_cast<int64_t>(t) * row;
+                float v[8];
+                if (tok < old) Vec8<ST>::load(staging + static_cast<int64_t>(t) * row + c, v);
+                else Vec8<NT>::load(src_new + static_cast<int64_t>(tok - old) * row + c, v);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) a = fmaxf(a, fabsf(v[i]));
+            }
+            a = block_max(a, red);
+            const double s = scale_from_absmax(a, INT4 ? 7.0 : 127.0);
+            const float sf = static_cast<float>(s);
+            if (threadIdx.x == 0) (kv ? p.v_scales : p.k_scales)[page] = sf;
+            uint8_t* pool = static_cast<uint8_t*>(kv ? p.v_pool : p.k_pool);
+            for (int64_t e = threadIdx.x * 8; e < pe; e += kAppendThreads * 8) {
+                const int t = static_cast<int>(e / row);
+                const int tok = page_start + t;
+                const int64_t c = e - static_cast<int64_t>(t) * row;
+                float v[8];
+                if (tok < old) Vec8<ST>::load(staging + static_cast<int64_t>(t) * row + c, v);
+                else Vec8<NT>::load(src_new + static_cast<int64_t>(tok - old) * row + c, v);
+                if (!INT4) {
+                    uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        w0 |= (static_cast<uint32_t>(quant_code(v[i], sf, 127.0f)) & 0xFFu) << (8 * i);
+                        w1 |= (static_cast<uint32_t>(quant_code(v[4 + i], sf, 127.0f)) & 0xFFu) << (8 * i);
+                    }
+                    *reinterpret_cast<uint2*>(pool + static_cast<int64_t>(page) * pe + e) = make_uint2(w0, w1);
+                } else {
+                    uint32_t w = 0;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        w |= (static_cast<uint32_t>(quant_code(v[i], sf, 7.0f)) & 0xFu) << (4 * i);
+                    *reinterpret_cast<uint32_t*>(pool + static_cast<int64_t>(page) * (pe / 2) + e / 2) = w;
+                }
+            }
+        }
+    }
+    // The first touched page's CTA is the only one that reads the old staged
+    // rows, so it also writes the new partial page's rows (after its reads).
+    if (jj == 0 && (jlast + 1) * P > new_len) {
+        __syncthreads();
+        const int first = old > jlast * P ? old : jlast * P;
+        const int64_t e0 = static_cast<int64_t>(first - jlast * P) * row;
+        const int64_t e1 = static_cast<int64_t>(new_len - jlast * P) * row;
+        for (int64_t e = e0 + threadIdx.x * 8; e < e1; e += kAppendThreads * 8) {
+            const int t = static_cast<int>(e / row);
+            const int64_t c = e - static_cast<int64_t>(t) * row;
+            float v[8];
+            Vec8<NT>::load(src_new + static_cast<int64_t>(jlast * P + t - old) * row + c, v);
+            Vec8<ST>::store(staging + e, v);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// gather + dequantize: one CTA per (logical page slot, sequence, K|V)
+// ---------------------------------------------------------------------------
+struct GatherParams {
+    const void* k_pool;
+    const void* v_pool;
+    const float* k_scales;
+    const float* v_scales;
+    const void* staging_k;
+    const void* staging_v;
+    const int32_t* block_tables;
+    int32_t max_blocks;
+    const int32_t* seq_lens;
+    const int32_t* cu_seqlens;
+    int32_t P;
+    int32_t row;
+    int64_t num_pages;
+    int32_t include_staging;
+    void* out_k;
+    void* out_v;
+    int32_t* status;
+};
+
+template <bool INT4, typename ST, typename OT>
+__global__ void __launch_bounds__(kGatherThreads) gather_dequant_kernel(GatherParams p) {
+    const int j = blockIdx.x, b = blockIdx.y, kv = blockIdx.z;
+    const int len = p.seq_lens[b];
+    const int P = p.P, row = p.row;
+    const int npages = len / P, tail = len % P;
+    const int64_t pe = static_cast<int64_t>(P) * row;
+    const int expect = p.include_staging ? len : npages * P;
+    if (p.cu_seqlens[b + 1] - p.cu_seqlens[b] != expect || npages > p.max_blocks) {
+        if (j == 0 && kv == 0 && threadIdx.x == 0) flag(p.status, MG_DEV_BAD_ARGUMENT);
+        return;
+    }
+    OT* out = static_cast<OT*>(kv ? p.out_v : p.out_k) + (static_cast<int64_t>(p.cu_seqlens[b]) + static_cast<int64_t>(j) * P) * row;
+    if (j < npages) {
+        int32_t page = p.block_tables[static_cast<int64_t>(b) * p.max_blocks + j];
+        if (page < 0 || page >= p.num_pages) {
+            if (threadIdx.x == 0) flag(p.status, MG_DEV_BAD_PAGE_ID);
+            page = 0;
+        }
+        const float sf = (kv ? p.v_scales : p.k_scales)[page];
+        const uint8_t* pool = static_cast<const uint8_t*>(kv ? p.v_pool : p.k_pool);
+        for (int64_t e = threadIdx.x * 8; e < pe; e += kGatherThreads * 8) {
+            float v[8];
+            if (!INT4) {
+                const uint2 w = *reinterpret_cast<const uint2*>(pool + static_cast<int64_t>(page) * pe + e);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    v[i] = static_cast<float>(static_cast<int8_t>(w.x >> (8 * i))) * sf;
+                    v[4 + i] = static_cast<float>(static_cast<int8_t>(w.y >> (8 * i))) * sf;
+                }
+            } else {
+                const uint32_t w = *reinterpret_cast<const uint32_t*>(pool + static_cast<int64_t>(page) * (pe / 2) + e / 2);
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    v[i] = static_cast<float>(static_cast<int>(static_cast<int8_t>((w >> (4 * i)) << 4)) >> 4) * sf;
+            }
+            Vec8<OT>::store(out + e, v);
+        }
+    } else if (j == npages && p.include_staging && tail > 0) {
+        const ST* st = static_cast<const ST*>(kv ? p.staging_v : p.staging_k) + static_cast<int64_t>(b) * pe;
+        for (int64_t e = threadIdx.x * 8; e < static_cast<int64_t>(tail) * row; e += kGatherThreads * 8) {
+            float v[8];
+            Vec8<ST>::load(st + e, v);
+            Vec8<OT>::store(out + e, v);
+        }
+    }
+}
+
+inline bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+mg_status check_layout(const mg_cache_layout* L) {
+    MG_REQUIRE(L != nullptr, "null layout");
+    MG_REQUIRE(L->kv_dtype == MG_KV_INT8 || L->kv_dtype == MG_KV_INT4, "kv_dtype must be MG_KV_INT8 or MG_KV_INT4");
+    MG_REQUIRE(L->staging_dtype == MG_F32 || L->staging_dtype == MG_F16, "staging_dtype must be MG_F32 or MG_F16");
+    MG_REQUIRE(L->page_size >= 1 && L->page_size <= 64, "page_size must be in [1, 64], got %d", L->page_size);
+    MG_REQUIRE(L->num_kv_heads >= 1, "num_kv_heads must be positive");
+    MG_REQUIRE(L->head_dim >= 8 && L->head_dim % 8 == 0, "head_dim must be a positive multiple of 8, got %d",
+               L->head_dim);
+    MG_REQUIRE(L->kv_dtype == MG_KV_INT8 || L->head_dim % 32 == 0,
+               "INT4 pools need head_dim % 32 == 0 (16-byte rows), got %d", L->head_dim);
+    MG_REQUIRE(L->max_blocks >= 1, "max_blocks must be positive");
+    MG_REQUIRE(L->num_pages >= 1 && L->num_pages < (1ll << 31), "num_pages out of range");
+    return MG_OK;
+}
+
+}  // namespace
+
+mg_status check_cache_layout(const mg_cache_layout* L) { return check_layout(L); }
+
+}  // namespace mg
+
+using namespace mg;
+
+extern "C" mg_status mg_alloc_init(const mg_allocator* a, mg_stream_t stream) {
+    MG_REQUIRE(a && a->free_stack && a->n_free && a->in_use, "null allocator pointer");
+    MG_REQUIRE(a->num_pages >= 1 && a->num_pages < (1ll << 31), "num_pages out of range");
+    const unsigned g = static_cast<unsigned>((a->num_pages + 255) / 256 > 4096 ? 4096 : (a->num_pages + 255) / 256);
+    alloc_init_kernel<<<g, 256, 0, as_stream(stream)>>>(a->free_stack, a->n_free, a->in_use, a->num_pages);
+    return check_launch("alloc_init_kernel");
+}
+
+extern "C" mg_status mg_plan_append(const mg_allocator* a, int32_t* block_tables, int32_t max_blocks,
+                                    int32_t* seq_lens, const int32_t* n_new, int32_t batch, int32_t page_size,
+                                    int32_t* dev_status, mg_stream_t stream) {
+    MG_REQUIRE(a && a->free_stack && a->n_free && a->in_use, "null allocator pointer");
+    MG_REQUIRE(batch >= 0, "batch must be >= 0");
+    if (batch == 0) return MG_OK;
+    MG_REQUIRE(block_tables && seq_lens && n_new, "null pointer");
+    MG_REQUIRE(page_size >= 1 && max_blocks >= 1, "page_size and max_blocks must be positive");
+    plan_append_kernel<<<1, kPlanThreads, 0, as_stream(stream)>>>(a->free_stack, a->n_free, a->in_use, block_tables,
+                                                                  max_blocks, seq_lens, n_new, batch, page_size,
+                                                                  dev_status);
+    return check_launch("plan_append_kernel");
+}
+
+extern "C" mg_status mg_free_sequences(const mg_allocator* a, const int32_t* block_tables, int32_t max_blocks,
+                                       int32_t* seq_lens, int32_t batch, const int32_t* seq_ids, int32_t num_seqs,
+                                       int32_t page_size, int32_t* dev_status, mg_stream_t stream) {
+    MG_REQUIRE(a && a->free_stack && a->n_free && a->in_use, "null allocator pointer");
+    MG_REQUIRE(num_seqs >= 0, "num_seqs must be >= 0");
+    if (num_seqs == 0) return MG_OK;
+    MG_REQUIRE(block_tables && seq_lens && seq_ids, "null pointer");
+    MG_REQUIRE(page_size >= 1, "page_size must be positive");
+    free_sequences_kernel<<<1, kPlanThreads, 0, as_stream(stream)>>>(a->free_stack, a->n_free, a->in_use,
+                                                                     a->num_pages, block_tables, max_blocks,
+                                                                     seq_lens, batch, seq_ids, num_seqs, page_size,
+                                                                     dev_status);
+    return check_launch("free_sequences_kernel");
+}
+
+extern "C" mg_status mg_kv_append(const mg_cache_layout* L, const mg_layer_ptrs* lp, const int32_t* block_tables,
+                                  const int32_t* seq_lens, const int32_t* n_new, int32_t batch, const void* k_new,
+                                  const void* v_new, int32_t new_dtype, int32_t max_new, int32_t* dev_status,
+                                  mg_stream_t stream) {
+    mg_status st = check_layout(L);
+    if (st != MG_OK) return st;
+    MG_REQUIRE(lp != nullptr, "null layer pointers");
+    MG_REQUIRE(batch >= 0 && max_new >= 0, "batch and max_new must be >= 0");
+    if (batch == 0 || max_new == 0) return MG_OK;
+    MG_REQUIRE(new_dtype == MG_F32 || new_dtype == MG_F16, "new_dtype must be MG_F32 or MG_F16");
+    MG_REQUIRE(!(new_dtype == MG_F32 && L->staging_dtype == MG_F16),
+               "fp32 tokens cannot be staged in an fp16 staging buffer without rounding");
+    MG_REQUIRE(lp->k_pool && lp->v_pool && lp->k_scales && lp->v_scales && lp->staging_k && lp->staging_v,
+               "null layer pointer");
+    MG_REQUIRE(k_new && v_new && block_tables && seq_lens && n_new, "null pointer");
+    MG_REQUIRE(aligned16(k_new) && aligned16(v_new) && aligned16(lp->staging_k) && aligned16(lp->staging_v) &&
+                   aligned16(lp->k_pool) && aligned16(lp->v_pool),
+               "k_new, v_new, staging and pools must be 16-byte aligned");
+    AppendParams p;
+    p.k_new = k_new;
+    p.v_new = v_new;
+    p.max_new = max_new;
+    p.k_pool = lp->k_pool;
+    p.v_pool = lp->v_pool;
+    p.k_scales = lp->k_scales;
+    p.v_scales = lp->v_scales;
+    p.staging_k = lp->staging_k;
+    p.staging_v = lp->staging_v;
+    p.block_tables = block_tables;
+    p.max_blocks = L->max_blocks;
+    p.seq_lens = seq_lens;
+    p.n_new = n_new;
+    p.P = L->page_size;
+    p.row = L->num_kv_heads * L->head_dim;
+    p.num_pages = L->num_pages;
+    p.status = dev_status;
+    const int touch = (max_new + L->page_size - 1) / L->page_size + 1;
+    dim3 grid(batch, touch, 2);
+    const bool i4 = L->kv_dtype == MG_KV_INT4;
+    const bool s16 = L->staging_dtype == MG_F16, n16 = new_dtype == MG_F16;
+    cudaStream_t s = as_stream(stream);
+    if (!i4 && s16 && n16) kv_append_kernel<false, __half, __half><<<grid, kAppendThreads, 0, s>>>(p);
+    else if (!i4 && !s16 && n16) kv_append_kernel<false, float, __half><<<grid, kAppendThreads, 0, s>>>(p);
+    else if (!i4 && !s16 && !n16) kv_append_kernel<false, float, float><<<grid, kAppendThreads, 0, s>>>(p);
+    else if (i4 && s16 && n16) kv_append_kernel<true, __half, __half><<<grid, kAppendThreads, 0, s>>>(p);
+    else if (i4 && !s16 && n16) kv_append_kernel<true, float, __half><<<grid, kAppendThreads, 0, s>>>(p);
+    else kv_append_kernel<true, float, float><<<grid, kAppendThreads, 0, s>>>(p);
+    return check_launch("kv_append_kernel");
+}
+
+extern "C" mg_status mg_gather_dequant(const mg_cache_layout* L, const mg_layer_ptrs* lp, const int32_t* block_tables,
+                                       const int32_t* seq_lens, const int32_t* cu_seqlens, int32_t batch,
+                                       int32_t max_context, int32_t include_staging, void* out_k, void* out_v,
+                                       int32_t out_dtype, int32_t* dev_status, mg_stream_t stream) {
+    mg_status st = check_layout(L);
+    if (st != MG_OK) return st;
+    MG_REQUIRE(lp != nullptr, "null layer pointers");
+    MG_REQUIRE(batch >= 0 && max_context >= 0, "batch and max_context must be >= 0");
+    if (batch == 0 || max_context == 0) return MG_OK;
+    MG_REQUIRE(out_dtype == MG_F32 || out_dtype == MG_F16, "out_dtype must be MG_F32 or MG_F16");
+    MG_REQUIRE(block_tables && seq_lens && cu_seqlens && out_k && out_v, "null pointer");
+    MG_REQUIRE(aligned16(out_k) && aligned16(out_v), "outputs must be 16-byte aligned");
+    GatherParams p;
+    p.k_pool = lp->k_pool;
+    p.v_pool = lp->v_pool;
+    p.k_scales = lp->k_scales;
+    p.v_scales = lp->v_scales;
+    p.staging_k = lp->staging_k;
+    p.staging_v = lp->staging_v;
+    p.block_tables = block_tables;
+    p.max_blocks = L->max_blocks;
+    p.seq_lens = seq_lens;
+    p.cu_seqlens = cu_seqlens;
+    p.P = L->page_size;
+    p.row = L->num_kv_heads * L->head_dim;
+    p.num_pages = L->num_pages;
+    p.include_staging = include_staging;
+    p.out_k = out_k;
+    p.out_v = out_v;
+    p.status = dev_status;
+    dim3 grid(max_context / L->page_size + 1, batch, 2);
+    const bool i4 = L->kv_dtype == MG_KV_INT4;
+    const bool s16 = L->staging_dtype == MG_F16, o16 = out_dtype == MG_F16;
+    cudaStream_t s = as_stream(stream);
+    if (!i4) {
+        if (s16 && o16) gather_dequant_kernel<false, __half, __half><<<grid, kGatherThreads, 0, s>>>(p);
+        else if (s16) gather_dequant_kernel<false, __half, float><<<grid, kGatherThreads, 0, s>>>(p);
+        else if (o16) gather_dequant_kernel<false, float, __half><<<grid, kGatherThreads, 0, s>>>(p);
+        else gather_dequant_kernel<false, float, float><<<grid, kGatherThreads, 0, s>>>(p);
+    } else {
+        if (s16 && o16) gather_dequant_kernel<true, __half, __half><<<grid, kGatherThreads, 0, s>>>(p);
+        else if (s16) gather_dequant_kernel<true, __half, float><<<grid, kGatherThreads, 0, s>>>(p);
+        else if (o16) gather_dequant_kernel<true, float, __half><<<grid, kGatherThreads, 0, s>>>(p);
+        else gather_dequant_kernel<true, float, float><<<grid, kGatherThreads, 0, s>>>(p);
+    }
+    return check_launch("gather_dequant_kernel");
+}

@@ -1,0 +1,209 @@
+// Shared device/host helpers for the sm_100a kernels of the paged KV-cache path.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "metagross_b200.h"
+
+namespace mg {
+
+// ---------------------------------------------------------------------------
+// host-side error reporting (thread-local message behind mg_last_error)
+// ---------------------------------------------------------------------------
+mg_status set_error(mg_status s, const char* fmt, ...);
+mg_status check_launch(const char* what);
+int sm_count();  // multiprocessors of the current device (cached per device)
+
+#define MG_REQUIRE(cond, ...)                                                  \
+    do {                                                                       \
+        if (!(cond)) return ::mg::set_error(MG_ERR_INVALID_ARGUMENT, __VA_ARGS__); \
+    } while (0)
+
+inline cudaStream_t as_stream(mg_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// ---------------------------------------------------------------------------
+// device-side status word
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void flag(int32_t* status, int32_t bits) {
+    if (status) atomicOr(status, bits);
+}
+
+// ---------------------------------------------------------------------------
+// quantization arithmetic, bit-exact with the reference kernels:
+//   code = NaN ? 0 : (int)roundf(fminf(qmax, fmaxf(-qmax, x / s)))
+// (csrc/quantize.cu:51-57, csrc/quantize_int4.cu:57-58).  x / s is the IEEE
+// round-to-nearest quotient (the reference builds without fast-math), made
+// explicit with __fdiv_rn so no compiler flag can turn it into a reciprocal.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int quant_code(float x, float s, float qmax) {
+    if (isnan(x)) return 0;
+    float k = fminf(qmax, fmaxf(-qmax, __fdiv_rn(x, s)));
+    return static_cast<int>(roundf(k));
+}
+
+// scale = absmax / qmax in double (csrc/quantize.cu:108-109), 1e-8 when the
+// absmax is not finite or <= 1e-12.
+__device__ __forceinline__ double scale_from_absmax(float a, double qmax) {
+    bool ok = isfinite(a) && a > 1e-12f;
+    return ok ? __ddiv_rn(static_cast<double>(a), qmax) : 1e-8;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Block-wide max of non-negative values (absmax); every thread gets the result.
+// scratch: >= 32 floats of shared memory.
+__device__ __forceinline__ float block_max(float v, float* scratch) {
+    v = warp_max(v);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __syncthreads();
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    const int nw = (blockDim.x + 31) >> 5;
+    float r = lane < nw ? scratch[lane] : 0.0f;
+    r = warp_max(r);
+    return r;
+}
+
+// ---------------------------------------------------------------------------
+// int8 / int4 -> fp16 conversion without I2F.
+// fp16 0x6400 is 1024.0 with a 10-bit mantissa of unit weight, so the half
+// with bit pattern 0x6400 | u (u in 0..255 after a sign flip, or a nibble) is
+// exactly 1024 + u; subtracting 1024 + bias gives the signed code exactly.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t lop3_and_xor(uint32_t a, uint32_t b, uint32_t c) {
+    // (a & b) ^ c in one LOP3 (immediate 0x6A = (A & B) ^ C)
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
+    // (a & b) | c, immediate 0xEA
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+__device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+__device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+
+// Bytes b_lo (bits 0-7) and b_hi (bits 16-23) of x, each a two's-complement
+// int8, to half2 (lo, hi).  Other bits of x are ignored.
+__device__ __forceinline__ uint32_t s8pair_to_half2(uint32_t x) {
+    const uint32_t h = lop3_and_xor(x, 0x00FF00FFu, 0x64806480u);  // 1024 + (b ^ 0x80) = 1152 + b
+    return hsub2_u32(h, 0x64806480u);                                // - 1152 (fp16 0x6480)
+}
+// Nibbles at bits 0-3 and 16-19 (two's complement int4) to half2.
+__device__ __forceinline__ uint32_t s4pair_lo_to_half2(uint32_t x_xored) {
+    // x_xored = x ^ 0x88888888 (offset binary); 0x6408 = 1032.0
+    const uint32_t h = lop3_and_or(x_xored, 0x000F000Fu, 0x64006400u);
+    return hsub2_u32(h, 0x64086408u);
+}
+// Nibbles at bits 4-7 and 20-23 to half2: (1024 + 16 u) / 16 - (64 + 8).
+__device__ __forceinline__ uint32_t s4pair_hi_to_half2(uint32_t x_xored) {
+    const uint32_t h = lop3_and_or(x_xored, 0x00F000F0u, 0x64006400u);
+    // fma(h, 1/16, -72): 0x2C00 = 0.0625, 0xD480 = -72.0
+    return hfma2_u32(h, 0x2C002C00u, 0xD480D480u);
+}
+
+// ---------------------------------------------------------------------------
+// warp-level tensor-core primitives (sm_80+ PTX, valid on sm_100a)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// 8x8 b16 transpose across the warp: lane 4r+c holds row r cols (2c, 2c+1);
+// afterwards it holds row r of the transpose.
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+    uint32_t r;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(r) : "r"(x));
+    return r;
+}
+
+__device__ __forceinline__ float ex2(float x) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier + bulk (TMA, non-tensor) copies, global -> shared
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+// One bounded attempt; true when the phase with the given parity completed.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n"
+        " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: gives up after max_tries attempts (each attempt itself is
+// time-limited by the hardware), so a lost copy can never hang the GPU.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t max_tries) {
+    for (uint32_t i = 0; i < max_tries; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+// 1-D bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned)
+// completing on `bar` (complete_tx).
+__device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+            smem_u32(dst_smem)),
+        "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Fast unsigned division by a runtime divisor d in [1, 2^16) for n < 2^16:
+// q = (n * m) >> 16 ... kept simple: magic m = ceil(2^32 / d), q = umulhi(n, m).
+// Exact for n, d < 2^16 (error term n*(m*d - 2^32)/2^32/d < 1/d).
+struct FastDiv {
+    uint32_t d, m;
+    __host__ __device__ FastDiv() : d(1), m(0) {}
+    __host__ explicit FastDiv(uint32_t div) : d(div), m(div == 1 ? 0u : (uint32_t)((0x100000000ull + div - 1) / div)) {}
+    __device__ __forceinline__ uint32_t div(uint32_t n) const { return d == 1 ? n : __umulhi(n, m); }
+};
+
+}  // namespace mg

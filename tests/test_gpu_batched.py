@@ -1,0 +1,220 @@
+"""Batched device-resident cache against the oracle's PagedCacheModel.
+
+Bit-exact after every step: pools (INT8 codes / packed INT4 nibbles), page
+scales, block tables (LIFO allocator order), sequence lengths, staged rows.
+Attention: max-abs within 2e-3 of float64 dequantize-then-attend for fp16
+outputs, 1e-3 for fp32.  The gather/dequantize kernel is
+bit-exact against the oracle's dequantization.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _cache_cls():
+    from metagross_b200.batched import BatchedPagedKVCache
+
+    return BatchedPagedKVCache
+
+
+def _assert_state_equal(cache, model, layer=0):
+    np.testing.assert_array_equal(cache.seq_lens.cpu().numpy(), model.seq_lens)
+    nb = model.num_blocks
+    bt = cache.block_tables.cpu().numpy()
+    for b in range(model.B):
+        np.testing.assert_array_equal(bt[b, :nb[b]], model.block_tables[b, :nb[b]], err_msg=f"block table {b}")
+    used = sorted({int(model.block_tables[b, j]) for b in range(model.B) for j in range(nb[b])})
+    kp = cache.k_pool[layer].cpu().numpy()
+    vp = cache.v_pool[layer].cpu().numpy()
+    ks = cache.k_scales[layer].cpu().numpy()
+    vs = cache.v_scales[layer].cpu().numpy()
+    for p in used:
+        np.testing.assert_array_equal(kp[p], model.k_pool[p], err_msg=f"k page {p}")
+        np.testing.assert_array_equal(vp[p], model.v_pool[p], err_msg=f"v page {p}")
+        assert ks[p] == model.k_scales[p] and vs[p] == model.v_scales[p]
+    stk = cache.staging_k[layer].float().cpu().numpy()
+    for b in range(model.B):
+        r = len(model.staging_k[b])
+        if r:
+            np.testing.assert_array_equal(stk[b, :r], np.stack(model.staging_k[b]).astype(np.float32))
+    assert cache.allocator.free_list() == model.free_list
+
+
+@pytest.mark.parametrize("kv", ["int8", "int4"])
+@pytest.mark.parametrize("P", [16, 4, 7])
+def test_append_steps_bit_exact(kv, P):
+    g = torch.Generator().manual_seed(11)
+    B, H, D = 5, 3, 64
+    cache = _cache_cls()(1, B, H, D, page_size=P, num_pages=200, max_blocks=40, kv_dtype=kv,
+                         staging_dtype=torch.float16)
+    model = O.PagedCacheModel(B, 200, P, H, D, kv_dtype=kv, staging_dtype=np.float16, max_blocks=40)
+    for step, T in enumerate([3, 1, 1, 17, 1, 40, 2, 1]):
+        n_new = torch.randint(0, T + 1, (B,), generator=g, dtype=torch.int32)
+        k = (torch.randn(B, T, H, D, generator=g) * 2).half()
+        v = (torch.randn(B, T, H, D, generator=g) * 2).half()
+        if step == 5:  # 1% outliers x8 as in the INT4 config
+            k[torch.rand(k.shape, generator=g) < 0.01] *= 8
+        cache.begin_step(n_new)
+        cache.append(0, k.cuda(), v.cuda())
+        model.append(k.numpy(), v.numpy(), n_new.numpy())
+        cache.check()
+        _assert_state_equal(cache, model)
+
+
+def test_decode_attention_matches_oracle_fp16_int8_mha():
+    g = torch.Generator().manual_seed(5)
+    B, H, D, P = 6, 12, 64, 16
+    cache = _cache_cls()(1, B, H, D, page_size=P, num_pages=B * 20, max_blocks=20, staging_dtype=torch.float16)
+    model = O.PagedCacheModel(B, B * 20, P, H, D, staging_dtype=np.float16, max_blocks=20)
+    lens = torch.tensor([1, 16, 17, 100, 255, 300], dtype=torch.int32)
+    k = torch.randn(B, 300, H, D, generator=g).half()
+    v = torch.randn(B, 300, H, D, generator=g).half()
+    cache.begin_step(lens)
+    cache.append(0, k.cuda(), v.cuda())
+    model.append(k.numpy(), v.numpy(), lens.numpy())
+    _assert_state_equal(cache, model)
+    for step in range(3):
+        q = torch.randn(B, H, D, generator=g).half()
+        out = cache.attend(0, q.cuda())
+        cache.check()
+        ref = model.attend(q.float().numpy(), 1.0 / 8)
+        err = np.abs(out.float().cpu().numpy() - ref).max()
+        assert err < 2e-3, err
+        kn = torch.randn(B, 1, H, D, generator=g).half()
+        vn = torch.randn(B, 1, H, D, generator=g).half()
+        cache.begin_step(1)
+        cache.append(0, kn.cuda(), vn.cuda())
+        model.append(kn.numpy(), vn.numpy())
+
+
+@pytest.mark.parametrize("kv", ["int8", "int4"])
+@pytest.mark.parametrize("hq,hkv", [(32, 4), (8, 8), (12, 4), (16, 2)])
+@pytest.mark.parametrize("qdt", [torch.float16, torch.float32])
+def test_decode_attention_gqa(kv, hq, hkv, qdt):
+    if qdt == torch.float32 and hq // hkv > 8:
+        pytest.skip("fp32 q supports groups <= 8")
+    g = torch.Generator().manual_seed(hq * 7 + hkv)
+    B, D, P = 4, 64, 16
+    cache = _cache_cls()(1, B, hkv, D, page_size=P, num_pages=B * 40, max_blocks=40, kv_dtype=kv,
+                         staging_dtype=torch.float32 if qdt == torch.float32 else torch.float16)
+    model = O.PagedCacheModel(B, B * 40, P, hkv, D, kv_dtype=kv, max_blocks=40)
+    lens = torch.randint(128, 600, (B,), generator=g, dtype=torch.int32)
+    k = torch.randn(B, 600, hkv, D, generator=g).to(qdt)
+    v = torch.randn(B, 600, hkv, D, generator=g).to(qdt)
+    out_mask = torch.rand(k.shape, generator=g) < 0.01
+    k[out_mask] *= 8
+    cache.begin_step(lens)
+    cache.append(0, k.cuda(), v.cuda())
+    model.append(k.float().numpy(), v.float().numpy(), lens.numpy())
+    q = torch.randn(B, hq, D, generator=g).to(qdt)
+    out = cache.attend(0, q.cuda())
+    cache.check()
+    ref = model.attend(q.float().numpy(), 1.0 / 8)
+    err = np.abs(out.float().cpu().numpy() - ref).max()
+    assert err < (2e-3 if qdt == torch.float16 else 1e-3), err
+
+
+@pytest.mark.parametrize("kv", ["int8", "int4"])
+def test_gather_dequant_bit_exact(kv):
+    g = torch.Generator().manual_seed(3)
+    B, H, D, P = 4, 4, 64, 16
+    cache = _cache_cls()(1, B, H, D, page_size=P, num_pages=64, max_blocks=16, kv_dtype=kv,
+                         staging_dtype=torch.float16)
+    model = O.PagedCacheModel(B, 64, P, H, D, kv_dtype=kv, staging_dtype=np.float16, max_blocks=16)
+    lens = torch.tensor([0, 5, 16, 77], dtype=torch.int32)
+    k = torch.randn(B, 77, H, D, generator=g).half()
+    v = torch.randn(B, 77, H, D, generator=g).half()
+    cache.begin_step(lens)
+    cache.append(0, k.cuda(), v.cuda())
+    model.append(k.numpy(), v.numpy(), lens.numpy())
+    ok, ov, cu = cache.gather(0, dtype=torch.float32)
+    for b in range(B):
+        sl = slice(int(cu[b]), int(cu[b + 1]))
+        np.testing.assert_array_equal(ok[sl].cpu().numpy(), model.dequantized_sequence(b, "k"))
+        np.testing.assert_array_equal(ov[sl].cpu().numpy(), model.dequantized_sequence(b, "v"))
+
+
+def test_free_and_reuse_is_lifo():
+    B, H, D, P = 3, 2, 64, 16
+    cache = _cache_cls()(1, B, H, D, page_size=P, num_pages=12, max_blocks=8)
+    model = O.PagedCacheModel(B, 12, P, H, D, staging_dtype=np.float16, max_blocks=8)
+    g = torch.Generator().manual_seed(1)
+    lens = torch.tensor([33, 50, 20], dtype=torch.int32)
+    k = torch.randn(B, 50, H, D, generator=g).half()
+    cache.begin_step(lens)
+    cache.append(0, k.cuda(), k.cuda())
+    model.append(k.numpy(), k.numpy(), lens.numpy())
+    cache.free([1, 0])
+    model.free_sequence(1)
+    model.free_sequence(0)
+    assert cache.allocator.free_list() == model.free_list
+    lens2 = torch.tensor([40, 17, 0], dtype=torch.int32)
+    cache.begin_step(lens2)
+    cache.append(0, k.cuda(), k.cuda())
+    model.append(k.numpy(), k.numpy(), lens2.numpy())
+    cache.check()
+    _assert_state_equal(cache, model)
+
+
+def test_out_of_pages_is_all_or_nothing():
+    B, H, D, P = 2, 2, 64, 16
+    cache = _cache_cls()(1, B, H, D, page_size=P, num_pages=3, max_blocks=8)
+    k = torch.randn(B, 64, H, D).half().cuda()
+    cache.begin_step(torch.tensor([32, 32], dtype=torch.int32))  # needs 4 pages, has 3
+    cache.append(0, k, k)
+    assert cache.seq_lens.tolist() == [0, 0]
+    assert cache.allocator.num_free == 3
+    with pytest.raises(RuntimeError, match="out of pages"):
+        cache.check()
+
+
+def test_double_free_flagged():
+    cache = _cache_cls()(1, 2, 2, 64, page_size=16, num_pages=8, max_blocks=4)
+    k = torch.randn(2, 16, 2, 64).half().cuda()
+    cache.begin_step(16)
+    cache.append(0, k, k)
+    bt = cache.block_tables.clone()
+    sl = cache.seq_lens.clone()
+    cache.free([0])
+    cache.seq_lens.copy_(sl)  # resurrect the length so the same page is freed again
+    cache.block_tables.copy_(bt)
+    cache.free([0])
+    with pytest.raises(RuntimeError, match="double free"):
+        cache.check()
+
+
+def test_full_size_config2_properties():
+    """Config-2 sizes (B=32, H=12, D=64, 1024 tokens, shuffled pool): the
+    output of a constant-V cache is that constant, and attention is invariant
+    to relabelling physical pages (permuting pool rows + block-table ids)."""
+    B, H, D, P, C = 32, 12, 64, 16, 1024
+    g = torch.Generator().manual_seed(2)
+    cache = _cache_cls()(1, B, H, D, page_size=P, num_pages=B * C // P + 64, max_blocks=C // P + 4)
+    k = torch.randn(B, C, H, D, generator=g).half()
+    v = torch.full((B, C, H, D), 0.75).half()
+    cache.begin_step(C)
+    cache.append(0, k.cuda(), v.cuda())
+    q = torch.randn(B, H, D, generator=g).half().cuda()
+    out = cache.attend(0, q)
+    cache.check()
+    assert torch.allclose(out.float(), torch.full_like(out.float(), 0.75), atol=1e-3)
+    # relabel pages: new_pool[perm[p]] = pool[p], block ids mapped through perm
+    v2 = torch.randn(B, C, H, D, generator=g).half()
+    cache.reset()
+    cache.begin_step(C)
+    cache.append(0, k.cuda(), v2.cuda())
+    out1 = cache.attend(0, q).float()
+    perm = torch.randperm(cache.num_pages, generator=g).cuda()
+    kp, vp = cache.k_pool[0].clone(), cache.v_pool[0].clone()
+    ks, vs = cache.k_scales[0].clone(), cache.v_scales[0].clone()
+    cache.k_pool[0][perm] = kp
+    cache.v_pool[0][perm] = vp
+    cache.k_scales[0][perm] = ks
+    cache.v_scales[0][perm] = vs
+    cache.block_tables.copy_(perm[cache.block_tables.long()].int())
+    out2 = cache.attend(0, q).float()
+    assert torch.equal(out1, out2)
