@@ -8,7 +8,11 @@ allocator/planner launch, then per layer the KV append of one new token per
 sequence (a page commit every 16 steps) and the fused attention.  The 12
 pools (~610 MB) exceed the 126 MB L2, so no flush is needed between steps.
 
-Contexts start at 1024 - W - 1 so the K timed steps run at 1024 .. 1024+K-1.
+Each sequence's context stays within one page of its configured length: it
+grows one token per step and every 16 steps its last page is truncated back
+to the allocator (a real cache operation, counted in the timed region), so
+the timed steps see contexts 1009..1024 (mean ~1016.5) with one page commit
+per sequence every 16 steps (at context 1024).
 
 Metric value = algorithmic HBM bytes of the step (codes, scales, block table,
 staged tail, q, out, append traffic; each byte counted once) / device time.
@@ -91,74 +95,124 @@ def append_bytes(lens_after, w):
 # --------------------------------------------------------------------------
 
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """Samples SM clock and throttle reasons with nvidia-smi every 50 ms while
+    the timed region runs (line-buffered through stdbuf; rows are kept only
+    between mark_start() and mark_stop())."""
 
-    def __init__(self, gpu_index):
-        self.idx = gpu_index
+    FIELDS = ("timestamp,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+
+    def __init__(self, device_index):
         self.proc = None
-        self.lines = []
+        self.rows = []
+        self.window = [None, None]
+        try:
+            p = torch.cuda.get_device_properties(device_index)
+            self.bus = f"{p.pci_bus_id:02x}:{p.pci_device_id:02x}".lower()
+        except Exception:
+            self.bus = None
 
     def start(self):
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50"]
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
+            self.proc = subprocess.Popen(["stdbuf", "-oL"] + cmd, stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+        time.sleep(0.3)  # first samples arrive before the timed region starts
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.rows.append((time.time(), line.strip()))
+
+    def mark_start(self):
+        self.window[0] = time.time()
+
+    def mark_stop(self):
+        self.window[1] = time.time()
 
     def stop(self):
         if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        time.sleep(0.12)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
+        t0, t1 = self.window
+        sm, smax, reasons, power = [], None, set(), []
+        for ts, ln in self.rows:
+            if t0 is not None and not (t0 - 0.06 <= ts <= (t1 or ts) + 0.06):
+                continue
+            parts = [x.strip() for x in ln.split(",")]
             if len(parts) < 9:
                 continue
+            if self.bus and self.bus not in parts[1].lower():
+                continue
             try:
-                sm.append(float(parts[1]))
-                smax = float(parts[2])
+                sm.append(float(parts[2]))
+                smax = float(parts[3])
+                power.append(float(parts[4]))
             except ValueError:
                 continue
-            for n, v in zip(names, parts[5:9]):
+            for n, v in zip(self.NAMES, parts[5:9]):
                 if v.lower() == "active":
                     reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_median": statistics.median(power) if power else None}
 
 
 # --------------------------------------------------------------------------
 # workload construction
 # --------------------------------------------------------------------------
 
-def contexts_for(w, batch, seed, start_offset):
+def contexts_for(w, batch, seed):
     g = torch.Generator().manual_seed(seed)
     if w["ctx"] == "uniform128_2048":
         c = torch.randint(128, 2049, (batch,), generator=g)
     else:
         c = torch.full((batch,), int(w["ctx"]))
-    return (c - start_offset).clamp(min=1).to(torch.int32)
+    return c.to(torch.int32)
 
 
-def build(w, warmup, steps, device, seed):
+class Schedule:
+    """Host shadow of the per-sequence lengths.  Sequence b oscillates in
+    (base_b, base_b + P]: it grows by one token per step and, once it reaches
+    base_b + P, is truncated back to the page boundary base_b (its last page
+    returns to the allocator) before the next step.  base_b = floor((c_b-1)/P)*P
+    for the workload's context c_b, so contexts stay within one page of c_b
+    and every sequence commits one page every P steps."""
+
+    def __init__(self, ctx, P):
+        self.P = P
+        self.base = ((ctx - 1) // P) * P
+        self.cur = ctx - 1  # prefilled length; the first step appends token c_b
+
+    def next_step(self):
+        """(truncate ids or None, new lens or None, lengths after the step)"""
+        hit = self.cur >= self.base + self.P
+        ids = lens = None
+        if bool(hit.any()):
+            ids = torch.nonzero(hit).flatten().to(torch.int32)
+            lens = self.base[hit].to(torch.int32)
+            self.cur = torch.where(hit, self.base, self.cur)
+        self.cur = self.cur + 1
+        return ids, lens, self.cur.clone()
+
+
+def build(w, device, seed):
     from metagross_b200.batched import BatchedPagedKVCache
 
     B, L, hkv, d, P, hq = w["batch"], w["layers"], w["hkv"], w["d"], w["page"], w["hq"]
-    start = contexts_for(w, B, seed, warmup + 1)
-    max_final = int(start.max()) + warmup + steps + 1
+    ctx = contexts_for(w, B, seed)
+    start = ctx - 1
+    max_final = int(ctx.max()) + P
     max_blocks = max_final // P + 2
     # pool with slack so physical pages come out of a shuffled free list
     num_pages = B * max_blocks + 256
@@ -183,22 +237,37 @@ def build(w, warmup, steps, device, seed):
         del k, v
     torch.cuda.synchronize()
     cache.check()
+    cache._max_len = max_final
     # per-step inputs (device), distinct per layer
     q = torch.randn(L, B, hq, d, generator=gd, device=device, dtype=torch.float16)
     kn = torch.randn(L, B, 1, hkv, d, generator=gd, device=device, dtype=torch.float16)
     vn = torch.randn(L, B, 1, hkv, d, generator=gd, device=device, dtype=torch.float16)
     out = torch.empty(L, B, hq, d, device=device, dtype=torch.float16)
-    return cache, start, q, kn, vn, out
+    return cache, Schedule(ctx, P), max_final, q, kn, vn, out
 
 
-def run_step(cache, q, kn, vn, out, ev=None):
+def plan_steps(sched, n, device):
+    """Precompute n steps of the schedule: device truncation args + host lengths after each step."""
+    plans = []
+    for _ in range(n):
+        ids, lens, after = sched.next_step()
+        if ids is not None:
+            ids, lens = ids.to(device), lens.to(device)
+        plans.append((ids, lens, after.tolist()))
+    return plans
+
+
+def run_step(cache, q, kn, vn, out, plan, max_context, ev=None):
     """One decode step over all layers; ev: list of (start, end) event pairs around each attention."""
+    ids, lens, _ = plan
+    if ids is not None:
+        cache.truncate(lens, ids)
     cache.begin_step(1)
     for layer in range(cache.num_layers):
         cache.append(layer, kn[layer], vn[layer])
         if ev is not None:
             ev[layer][0].record()
-        cache.attend(layer, q[layer], out=out[layer], max_context=cache._max_len)
+        cache.attend(layer, q[layer], out=out[layer], max_context=max_context)
         if ev is not None:
             ev[layer][1].record()
 
@@ -245,8 +314,8 @@ def traffic_per_launch(workload):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=30)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="gpt2_int8")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -281,50 +350,56 @@ def main():
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
 
-    cache, start, q, kn, vn, out = build(w, args.warmup, args.steps, device, seed=1234 + rank)
+    cache, sched, max_ctx, q, kn, vn, out = build(w, device, seed=1234 + rank)
     L, B = w["layers"], w["batch"]
     gather_buf = None
     if world > 1:
         gather_buf = torch.empty(world * B, w["hq"], w["d"], device=device, dtype=torch.float16)
+    e2e_steps = max(3, args.steps // 2)
+    warm_plans = plan_steps(sched, args.warmup, device)
+    timed_plans = plan_steps(sched, args.steps, device)
+    e2e_plans = plan_steps(sched, e2e_steps, device)
 
-    def step(ev=None):
-        run_step(cache, q, kn, vn, out, ev)
+    def step(plan, ev=None, qq=q, kk=kn, vv=vn):
+        run_step(cache, qq, kk, vv, out, plan, max_ctx, ev)
         if world > 1:
             import torch.distributed as dist
 
             dist.all_gather_into_tensor(gather_buf, out[L - 1])
 
-    for _ in range(args.warmup):
-        step()
+    for pl in warm_plans:
+        step(pl)
     torch.cuda.synchronize()
     cache.check()
 
-    # bytes of the timed steps (contexts known on the host)
-    lens0 = start + args.warmup  # lengths before the first timed step
+    # bytes of the timed steps (lengths known on the host)
     att_b, app_b = 0.0, 0.0
-    for s in range(args.steps):
-        after = (lens0 + s + 1).tolist()
+    n_trunc = 0
+    for ids, _, after in timed_plans:
         att_b += L * attention_bytes(after, w)
         app_b += L * append_bytes(after, w)
+        n_trunc += ids is not None
     step_bytes = (att_b + app_b) / args.steps
     att_bytes_per_launch = att_b / (args.steps * L)
 
     ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
           for _ in range(args.steps)]
     clocks = ClockSampler(local)
+    clocks.start()
     if world > 1:
         import torch.distributed as dist
 
         dist.barrier()
     torch.cuda.synchronize()
-    clocks.start()
+    clocks.mark_start()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record()
     for s in range(args.steps):
-        step(ev[s])
+        step(timed_plans[s], ev[s])
     t1.record()
     torch.cuda.synchronize()
+    clocks.mark_stop()
     clk = clocks.stop()
     ms = t0.elapsed_time(t1)
     att_ms = [ev[s][l][0].elapsed_time(ev[s][l][1]) for s in range(args.steps) for l in range(L)]
@@ -338,50 +413,41 @@ def main():
     cache.check()
 
     # ---- end to end through the public API with host buffers -----------------
-    e2e = None
-    if True:
-        qh = q.cpu().pin_memory()
-        knh, vnh = kn.cpu().pin_memory(), vn.cpu().pin_memory()
-        outh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-        qd, knd, vnd = torch.empty_like(q), torch.empty_like(kn), torch.empty_like(vn)
-        e2e_steps = max(3, args.steps // 2)
-        lens_e = (lens0 + args.steps).clone()
-        e_bytes = 0.0
-        for s in range(e2e_steps):
-            after = (lens_e + s + 1).tolist()
-            e_bytes += L * (attention_bytes(after, w) + append_bytes(after, w))
-        if world > 1:
-            import torch.distributed as dist
+    qh = q.cpu().pin_memory()
+    knh, vnh = kn.cpu().pin_memory(), vn.cpu().pin_memory()
+    outh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    qd, knd, vnd = torch.empty_like(q), torch.empty_like(kn), torch.empty_like(vn)
+    e_bytes = 0.0
+    for _, _, after in e2e_plans:
+        e_bytes += L * (attention_bytes(after, w) + append_bytes(after, w))
+    if world > 1:
+        import torch.distributed as dist
 
-            dist.barrier()
-        torch.cuda.synchronize()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for s in range(e2e_steps):
-            qd.copy_(qh, non_blocking=True)
-            knd.copy_(knh, non_blocking=True)
-            vnd.copy_(vnh, non_blocking=True)
-            run_step(cache, qd, knd, vnd, out)
-            if world > 1:
-                import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for s in range(e2e_steps):
+        qd.copy_(qh, non_blocking=True)
+        knd.copy_(knh, non_blocking=True)
+        vnd.copy_(vnh, non_blocking=True)
+        step(e2e_plans[s], None, qd, knd, vnd)
+        outh.copy_(out, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        import torch.distributed as dist
 
-                dist.all_gather_into_tensor(gather_buf, out[L - 1])
-            outh.copy_(out, non_blocking=True)
-        e1.record()
-        torch.cuda.synchronize()
-        e_ms = e0.elapsed_time(e1)
-        if world > 1:
-            import torch.distributed as dist
-
-            t = torch.tensor([e_ms], device=device)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e_ms = float(t[0])
-        e2e = {"value": world * e_bytes / (e_ms / 1e3) / 1e9, "unit": "GB/s",
-               "h2d_bytes_per_step": int(q.numel() * 2 + kn.numel() * 2 + vn.numel() * 2),
-               "d2h_bytes_per_step": int(out.numel() * 2),
-               "ms_per_step": e_ms / e2e_steps}
-        cache.check()
+        t = torch.tensor([e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_ms = float(t[0])
+    e2e = {"value": round(world * e_bytes / (e_ms / 1e3) / 1e9, 1), "unit": "GB/s",
+           "h2d_bytes_per_step": int(q.numel() * 2 + kn.numel() * 2 + vn.numel() * 2),
+           "d2h_bytes_per_step": int(out.numel() * 2), "ms_per_step": e_ms / e2e_steps}
+    cache.check()
+    ctx_mean = float(np.mean([np.mean(a) for _, _, a in timed_plans]))
 
     if rank == 0:
         peak, peak_kind = peaks()
@@ -393,7 +459,7 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": w["kv"] if w["kv"] == "int8" else "int4", "data": "synthetic",
             "config": {"workload": args.workload, "desc": w["desc"], "global_batch": world * B,
-                       "context_mean": float((lens0 + (args.steps + 1) / 2).float().mean()),
+                       "context_mean": round(ctx_mean, 1), "truncations_timed": n_trunc,
                        "layers": L, "parallelism": f"sequence-sharded dp{world}",
                        "l2": "working set per step > 126 MB L2 (one pool per layer); no flush"},
             "decode_tokens_per_s": round(tok_s, 1),
@@ -404,7 +470,7 @@ def main():
                          "kernel": "paged_decode_kernel", "algorithmic_bytes_per_launch": att_bytes_per_launch,
                          "avg_launch_ms": att_avg_ms},
             "e2e": e2e,
-            "gpu_launches": args.steps * (1 + 2 * L),
+            "gpu_launches": args.steps * (1 + 2 * L) + n_trunc,
             "clocks": clk,
         }
         if world == 1 and not args.no_cpu_baseline:

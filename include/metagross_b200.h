@@ -198,7 +198,11 @@ MG_API mg_status mg_kv_append(const mg_cache_layout* layout, const mg_layer_ptrs
  * the context with an in-kernel merge.  q [batch, num_q_heads, D] (q_dtype),
  * out [batch, num_q_heads, D] (out_dtype) = softmax(scale * q K^T) V.
  * max_context bounds seq_lens (0: max_blocks*page_size + page_size - 1).
- * workspace: mg_paged_decode_workspace_bytes(), zeroed before first use. */
+ * workspace: mg_paged_decode_workspace_bytes() bytes.  Its first
+ * 256*ceil(4*batch/256) bytes are per-sequence merge counters that must be
+ * zero before the first call; every call leaves them zero, so one zeroed
+ * buffer can serve calls of any max_context and head count.  Calls that share
+ * a workspace must not overlap on the device. */
 MG_API mg_status mg_paged_decode_attention(const mg_cache_layout* layout, const mg_layer_ptrs* layer,
                                     const int32_t* block_tables, const int32_t* seq_lens,
                                     int32_t batch, const void* q, int32_t q_dtype,
@@ -228,6 +232,18 @@ MG_API mg_status mg_free_sequences(const mg_allocator* alloc, const int32_t* blo
                                    int32_t max_blocks, int32_t* seq_lens, int32_t batch,
                                    const int32_t* seq_ids, int32_t num_seqs, int32_t page_size,
                                    int32_t* dev_status, mg_stream_t stream);
+
+/* Truncate the listed sequences to new_lens (in list order): pages at
+ * logical index >= new_len/page_size go back to the allocator in block-table
+ * order.  A new length must not cut a committed page in two (new_len %
+ * page_size == 0, or new_len >= the sequence's committed tokens); such a
+ * request sets MG_DEV_BAD_ARGUMENT and leaves that sequence unchanged.
+ * mg_free_sequences is truncation to 0. */
+MG_API mg_status mg_truncate_sequences(const mg_allocator* alloc, const int32_t* block_tables,
+                                       int32_t max_blocks, int32_t* seq_lens, int32_t batch,
+                                       const int32_t* seq_ids, const int32_t* new_lens,
+                                       int32_t num_seqs, int32_t page_size, int32_t* dev_status,
+                                       mg_stream_t stream);
 
 #ifdef __cplusplus
 }

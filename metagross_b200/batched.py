@@ -167,6 +167,22 @@ class BatchedPagedKVCache:
         _get_C().free_sequences(self.allocator.free_stack, self.allocator.n_free, self.allocator.in_use,
                                 self.block_tables, self.seq_lens, ids, self.page_size, self.status)
 
+    def truncate(self, new_lens, seq_ids=None) -> None:
+        """Shrink sequences to new_lens (int or per-sequence), freeing whole trailing pages.
+
+        A new length may not cut a committed page (multiple of page_size, or within
+        the staged tail); pages go back to the allocator in block-table order."""
+        if seq_ids is None:
+            seq_ids = torch.arange(self.batch, dtype=torch.int32)
+        ids = torch.as_tensor(seq_ids, dtype=torch.int32)
+        if isinstance(new_lens, int):
+            nl = torch.full((ids.numel(),), new_lens, dtype=torch.int32)
+        else:
+            nl = torch.as_tensor(new_lens, dtype=torch.int32)
+        _get_C().truncate_sequences(self.allocator.free_stack, self.allocator.n_free, self.allocator.in_use,
+                                    self.block_tables, self.seq_lens, ids.to(self.device), nl.to(self.device),
+                                    self.page_size, self.status)
+
     def reset(self) -> None:
         self.allocator.reset()
         self.seq_lens.zero_()

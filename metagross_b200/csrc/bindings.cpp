@@ -381,6 +381,23 @@ void kv_append(torch::Tensor k_pool, torch::Tensor v_pool, torch::Tensor k_scale
                  "kv_append");
 }
 
+void truncate_sequences(torch::Tensor free_stack, torch::Tensor n_free, torch::Tensor in_use,
+                        torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor seq_ids,
+                        torch::Tensor new_lens, int64_t page_size, c10::optional<torch::Tensor> status) {
+    const c10::cuda::CUDAGuard guard(free_stack.device());
+    auto a = make_alloc(free_stack, n_free, in_use);
+    check_i32_vec(block_tables, 1, "block_tables");
+    check_i32_vec(seq_lens, block_tables.size(0), "seq_lens");
+    check_i32_vec(seq_ids, 0, "seq_ids");
+    check_i32_vec(new_lens, seq_ids.numel(), "new_lens");
+    check_status(mg_truncate_sequences(&a, block_tables.data_ptr<int32_t>(),
+                                       static_cast<int32_t>(block_tables.size(1)), seq_lens.data_ptr<int32_t>(),
+                                       static_cast<int32_t>(block_tables.size(0)), seq_ids.data_ptr<int32_t>(),
+                                       new_lens.data_ptr<int32_t>(), static_cast<int32_t>(seq_ids.numel()),
+                                       static_cast<int32_t>(page_size), status_ptr(status), cur_stream()),
+                 "truncate_sequences");
+}
+
 int64_t decode_workspace_bytes(torch::Tensor k_pool, torch::Tensor block_tables, int64_t num_q_heads,
                                int64_t max_context) {
     mg_cache_layout L{};
@@ -466,6 +483,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("free_sequences", &free_sequences, "Free all pages of the listed sequences", pybind11::arg("free_stack"),
           pybind11::arg("n_free"), pybind11::arg("in_use"), pybind11::arg("block_tables"), pybind11::arg("seq_lens"),
           pybind11::arg("seq_ids"), pybind11::arg("page_size"), pybind11::arg("status") = pybind11::none());
+    m.def("truncate_sequences", &truncate_sequences, "Truncate sequences, freeing whole trailing pages",
+          pybind11::arg("free_stack"), pybind11::arg("n_free"), pybind11::arg("in_use"),
+          pybind11::arg("block_tables"), pybind11::arg("seq_lens"), pybind11::arg("seq_ids"),
+          pybind11::arg("new_lens"), pybind11::arg("page_size"), pybind11::arg("status") = pybind11::none());
     m.def("kv_append", &kv_append, "Write a step's K/V tokens: commit filled pages, stage the rest",
           pybind11::arg("k_pool"), pybind11::arg("v_pool"), pybind11::arg("k_scales"), pybind11::arg("v_scales"),
           pybind11::arg("staging_k"), pybind11::arg("staging_v"), pybind11::arg("block_tables"),

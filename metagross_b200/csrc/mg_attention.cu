@@ -690,7 +690,9 @@ mg_status make_plan(int kv4, int hd, int P, int Hkv, int Hq, int q_f16, int batc
     pl.nstages = nst;
     pl.smem_bytes = nst * stage;
     const int64_t S = pl.num_splits;
-    pl.ws_bytes = S > 1 ? align_up(static_cast<int64_t>(batch) * S * Hq * (hd + 2) * 4, 256) + align_up(batch * 4, 256)
+    // [per-sequence tickets][acc][m][l]: the tickets sit at a fixed offset so
+    // that calls with different split counts keep finding them at zero
+    pl.ws_bytes = S > 1 ? align_up(static_cast<int64_t>(batch) * 4, 256) + static_cast<int64_t>(batch) * S * Hq * (hd + 2) * 4
                         : 0;
     *out = pl;
     return MG_OK;
@@ -753,11 +755,11 @@ void set_workspace(DecodeParams& p, const Plan& pl, int batch, int Hq, int hd, v
         return;
     }
     const int64_t n = static_cast<int64_t>(batch) * pl.num_splits * Hq;
-    float* f = static_cast<float*>(ws);
+    p.tickets = static_cast<uint32_t*>(ws);
+    float* f = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + align_up(static_cast<int64_t>(batch) * 4, 256));
     p.ws_acc = f;
     p.ws_m = f + n * hd;
     p.ws_l = p.ws_m + n;
-    p.tickets = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ws) + align_up(n * (hd + 2) * 4, 256));
 }
 
 }  // namespace

@@ -119,13 +119,16 @@ __global__ void __launch_bounds__(kPlanThreads) plan_append_kernel(int32_t* free
     if (threadIdx.x == 0) *n_free_p = n_free - total;
 }
 
-// Frees the listed sequences' pages in (list order, block-table order).
+// Frees the listed sequences' pages beyond new_lens (0 when new_lens is
+// null) in (list order, block-table order): the order in which the
+// reference's BlockAllocator.free would be called.
 __global__ void __launch_bounds__(kPlanThreads) free_sequences_kernel(int32_t* free_stack, int32_t* n_free_p,
                                                                       int32_t* in_use, int64_t num_pages,
                                                                       const int32_t* block_tables,
                                                                       int32_t max_blocks, int32_t* seq_lens,
                                                                       int32_t batch, const int32_t* seq_ids,
-                                                                      int32_t num_seqs, int32_t P, int32_t* status) {
+                                                                      const int32_t* new_lens, int32_t num_seqs,
+                                                                      int32_t P, int32_t* status) {
     __shared__ int scratch[33];
     int top = *n_free_p;
     for (int i = 0; i < num_seqs; ++i) {
@@ -134,10 +137,18 @@ __global__ void __launch_bounds__(kPlanThreads) free_sequences_kernel(int32_t* f
             if (threadIdx.x == 0) flag(status, MG_DEV_BAD_ARGUMENT);
             continue;
         }
-        int npages = seq_lens[s] / P;
+        const int old_len = seq_lens[s];
+        const int new_len = new_lens ? new_lens[i] : 0;
+        const int committed = (old_len / P) * P;
+        if (new_len < 0 || new_len > old_len || (new_len % P != 0 && new_len < committed)) {
+            if (threadIdx.x == 0) flag(status, MG_DEV_BAD_ARGUMENT);
+            continue;
+        }
+        int npages = old_len / P;
         if (npages > max_blocks) npages = max_blocks;
+        const int keep = new_len / P;
         const int32_t* row = block_tables + static_cast<int64_t>(s) * max_blocks;
-        for (int start = 0; start < npages; start += blockDim.x) {
+        for (int start = keep; start < npages; start += blockDim.x) {
             const int j = start + threadIdx.x;
             int ok = 0;
             int32_t page = -1;
@@ -157,7 +168,7 @@ __global__ void __launch_bounds__(kPlanThreads) free_sequences_kernel(int32_t* f
             top += cnt;
         }
         __syncthreads();
-        if (threadIdx.x == 0) seq_lens[s] = 0;
+        if (threadIdx.x == 0) seq_lens[s] = new_len;
     }
     if (threadIdx.x == 0) *n_free_p = top;
 }
@@ -424,19 +435,27 @@ extern "C" mg_status mg_plan_append(const mg_allocator* a, int32_t* block_tables
     return check_launch("plan_append_kernel");
 }
 
-extern "C" mg_status mg_free_sequences(const mg_allocator* a, const int32_t* block_tables, int32_t max_blocks,
-                                       int32_t* seq_lens, int32_t batch, const int32_t* seq_ids, int32_t num_seqs,
-                                       int32_t page_size, int32_t* dev_status, mg_stream_t stream) {
+extern "C" mg_status mg_truncate_sequences(const mg_allocator* a, const int32_t* block_tables, int32_t max_blocks,
+                                           int32_t* seq_lens, int32_t batch, const int32_t* seq_ids,
+                                           const int32_t* new_lens, int32_t num_seqs, int32_t page_size,
+                                           int32_t* dev_status, mg_stream_t stream) {
     MG_REQUIRE(a && a->free_stack && a->n_free && a->in_use, "null allocator pointer");
     MG_REQUIRE(num_seqs >= 0, "num_seqs must be >= 0");
     if (num_seqs == 0) return MG_OK;
     MG_REQUIRE(block_tables && seq_lens && seq_ids, "null pointer");
-    MG_REQUIRE(page_size >= 1, "page_size must be positive");
+    MG_REQUIRE(page_size >= 1 && max_blocks >= 1 && batch >= 1, "page_size, max_blocks and batch must be positive");
     free_sequences_kernel<<<1, kPlanThreads, 0, as_stream(stream)>>>(a->free_stack, a->n_free, a->in_use,
                                                                      a->num_pages, block_tables, max_blocks,
-                                                                     seq_lens, batch, seq_ids, num_seqs, page_size,
-                                                                     dev_status);
+                                                                     seq_lens, batch, seq_ids, new_lens, num_seqs,
+                                                                     page_size, dev_status);
     return check_launch("free_sequences_kernel");
+}
+
+extern "C" mg_status mg_free_sequences(const mg_allocator* a, const int32_t* block_tables, int32_t max_blocks,
+                                       int32_t* seq_lens, int32_t batch, const int32_t* seq_ids, int32_t num_seqs,
+                                       int32_t page_size, int32_t* dev_status, mg_stream_t stream) {
+    return mg_truncate_sequences(a, block_tables, max_blocks, seq_lens, batch, seq_ids, nullptr, num_seqs,
+                                 page_size, dev_status, stream);
 }
 
 extern "C" mg_status mg_kv_append(const mg_cache_layout* L, const mg_layer_ptrs* lp, const int32_t* block_tables,

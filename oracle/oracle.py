@@ -254,6 +254,25 @@ class PagedCacheModel:
         self.staging_k[b] = []
         self.staging_v[b] = []
 
+    def truncate(self, b: int, new_len: int):
+        """Drop seq b's tokens beyond new_len (a page boundary, or inside the
+        staged tail); freed pages return to the pool in block-table order."""
+        old = int(self.seq_lens[b])
+        committed = (old // self.P) * self.P
+        assert 0 <= new_len <= old and (new_len % self.P == 0 or new_len >= committed)
+        keep = new_len // self.P
+        for j in range(keep, int(self.num_blocks[b])):
+            self.free_list.append(int(self.block_tables[b, j]))
+        if new_len < committed:
+            self.staging_k[b] = []
+            self.staging_v[b] = []
+        else:
+            r = new_len - committed
+            self.staging_k[b] = self.staging_k[b][:r]
+            self.staging_v[b] = self.staging_v[b][:r]
+        self.num_blocks[b] = keep
+        self.seq_lens[b] = new_len
+
     def _commit(self, b: int):
         m = self._allocate()
         j = int(self.num_blocks[b])

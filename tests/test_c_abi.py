@@ -14,7 +14,7 @@ LIB = os.path.join(ROOT, "metagross_b200", "libmgb200.so")
 
 REFERENCE_OPS = ["add", "quantize_new_scale", "quantize_fixed_scale", "dequantize_page", "paged_attention_committed",
                  "quantize_int4_new_scale", "dequantize_int4_page"]
-BATCHED_OPS = ["alloc_init", "plan_append", "free_sequences", "kv_append", "decode_workspace_bytes",
+BATCHED_OPS = ["alloc_init", "plan_append", "free_sequences", "truncate_sequences", "kv_append", "decode_workspace_bytes",
                "paged_decode_attention", "gather_dequant"]
 
 
@@ -28,7 +28,7 @@ def test_header_declares_the_boundary():
     for s in ["mg_quantize_int8_new_scale", "mg_quantize_int8_fixed_scale", "mg_dequantize_int8_page",
               "mg_quantize_int4_new_scale", "mg_dequantize_int4_page", "mg_paged_attention_committed",
               "mg_add_f32", "mg_plan_append", "mg_kv_append", "mg_paged_decode_attention", "mg_gather_dequant",
-              "mg_alloc_init", "mg_free_sequences"]:
+              "mg_alloc_init", "mg_free_sequences", "mg_truncate_sequences"]:
         assert s in syms, s
 
 

@@ -218,3 +218,46 @@ def test_full_size_config2_properties():
     cache.block_tables.copy_(perm[cache.block_tables.long()].int())
     out2 = cache.attend(0, q).float()
     assert torch.equal(out1, out2)
+
+
+def test_truncate_then_regrow_matches_oracle():
+    """Truncation frees trailing pages in block-table order (LIFO reuse), keeps a
+    staged-tail prefix, and later commits reuse the freed ids as the reference
+    allocator would."""
+    B, H, D, P = 3, 2, 64, 16
+    cache = _cache_cls()(1, B, H, D, page_size=P, num_pages=24, max_blocks=8)
+    model = O.PagedCacheModel(B, 24, P, H, D, staging_dtype=np.float16, max_blocks=8)
+    g = torch.Generator().manual_seed(4)
+    k = torch.randn(B, 70, H, D, generator=g).half()
+    v = torch.randn(B, 70, H, D, generator=g).half()
+    lens = torch.tensor([70, 37, 48], dtype=torch.int32)
+    cache.begin_step(lens)
+    cache.append(0, k.cuda(), v.cuda())
+    model.append(k.numpy(), v.numpy(), lens.numpy())
+    new = [32, 36, 0]  # page boundary, inside the staged tail, everything
+    cache.truncate(new)
+    for b, n in enumerate(new):
+        model.truncate(b, n)
+    cache.check()
+    _assert_state_equal(cache, model)
+    k2 = torch.randn(B, 40, H, D, generator=g).half()
+    grow = torch.tensor([40, 30, 17], dtype=torch.int32)
+    cache.begin_step(grow)
+    cache.append(0, k2.cuda(), k2.cuda())
+    model.append(k2.numpy(), k2.numpy(), grow.numpy())
+    cache.check()
+    _assert_state_equal(cache, model)
+    q = torch.randn(B, 4, D, generator=g).half()
+    err = np.abs(cache.attend(0, q.cuda()).float().cpu().numpy() - model.attend(q.float().numpy(), 0.125)).max()
+    assert err < 2e-3
+
+
+def test_truncate_rejects_cutting_a_committed_page():
+    cache = _cache_cls()(1, 1, 2, 64, page_size=16, num_pages=8, max_blocks=4)
+    k = torch.randn(1, 40, 2, 64).half().cuda()
+    cache.begin_step(40)
+    cache.append(0, k, k)
+    cache.truncate([20])  # inside committed page 1
+    assert cache.seq_lens.tolist() == [40]
+    with pytest.raises(RuntimeError, match="inconsistent"):
+        cache.check()
