@@ -55,7 +55,7 @@ typedef enum mg_status {
 #define MG_DEV_TIMEOUT 0x8           /* a bounded wait on a bulk copy gave up; output invalid */
 #define MG_DEV_BLOCK_TABLE_FULL 0x10 /* mg_plan_append: a sequence would outgrow its block-table row */
 #define MG_DEV_SKIPPED 0x20          /* a kernel skipped its work because an earlier bit was set */
-#define MG_DEV_CONTEXT_OVERFLOW 0x40 /* attention: a sequence is longer than the call's max_context; output not written */
+#define MG_DEV_CONTEXT_OVERFLOW 0x40 /* reserved (no current kernel sets it) */
 #define MG_DEV_BAD_ARGUMENT 0x80     /* a per-sequence argument (n_new > max_new, seq id, cu_seqlens) was inconsistent; that sequence was skipped */
 
 typedef enum mg_kv_dtype { MG_KV_INT8 = 0, MG_KV_INT4 = 1 } mg_kv_dtype;
@@ -197,7 +197,8 @@ MG_API mg_status mg_kv_append(const mg_cache_layout* layout, const mg_layer_ptrs
  * the block table plus the exact staged tail, one online softmax, split over
  * the context with an in-kernel merge.  q [batch, num_q_heads, D] (q_dtype),
  * out [batch, num_q_heads, D] (out_dtype) = softmax(scale * q K^T) V.
- * max_context bounds seq_lens (0: max_blocks*page_size + page_size - 1).
+ * The work is split evenly over the GPU by pages (stream-K), so no length
+ * bound is needed: max_context is accepted for compatibility and ignored.
  * workspace: mg_paged_decode_workspace_bytes() bytes.  Its first
  * 256*ceil(4*batch/256) bytes are per-sequence merge counters that must be
  * zero before the first call; every call leaves them zero, so one zeroed

@@ -1,0 +1,257 @@
+// Fused paged decode attention: kernel template and host-side plan.
+//
+// Reference semantics: csrc/paged_attention.cu:25-135 (committed INT8 pages,
+// one query per head, unnormalised (wv, sum, max) outputs) and
+// metagross/attention.py:62-134 (exact staged tail merged with a log-sum-exp
+// merge, then normalised).  Here one kernel does all of it for a batch:
+//
+//   work    stream-K over the flattened list of "units" (one committed page,
+//           or the staged tail, of one sequence): CTA c of G processes units
+//           [c*W/G, (c+1)*W/G), so every CTA streams the same number of pages
+//           whatever the context lengths.  A sequence cut by a CTA boundary
+//           gets a partial (m, l, acc) from each covering CTA; the last of
+//           them to finish (atomic ticket, no waiting) merges and writes the
+//           output.  Each CTA writes at most two partials (its first and its
+//           last sequence), so the workspace is O(G), not O(batch).
+//   data    no staging through shared memory for the pages: every warp loads
+//           its own 16-token tiles (one kv head's rows of K and V) straight
+//           from HBM into the registers in the tensor-core fragment layout,
+//           one (INT8) or two (INT4) tiles ahead of the math, so 16 warps per
+//           SM keep 32-64 KB of page data in flight.  The page ids and scales
+//           of a warp's next 32 tiles sit one per lane and travel by shuffle.
+//           A sequence's staged tail (< P exact fp16/fp32 rows, all heads) is
+//           copied to shared memory with cp.async when its segment starts and
+//           is folded in after the pages.
+//   warps   each warp owns one kv head (two when there are more kv heads than
+//           warps); when the model has few kv heads, WPH warps share a head
+//           and take alternate tiles, merging their softmax states in shared
+//           memory at the end of a sequence.
+//   math    per 16-token tile, S^T = K Q^T and O^T += V^T P^T on the tensor
+//           cores (mma.sync m16n8k16, fp16 in, fp32 accumulate).  INT8/INT4
+//           codes are exact in fp16 and are converted in registers with the
+//           0x6400 exponent trick (no I2F).  The K page scale multiplies the
+//           fp32 scores; the V page scale is folded into P.  For fp32 queries
+//           and small GQA groups (G <= 4) q and P travel as hi+lo fp16 pairs
+//           in two mma columns (~22 mantissa bits).  Online softmax in the
+//           log2 domain with lazy rescaling (the running reference max moves
+//           only when a score exceeds it by 2^8).
+//   tail    the staged tokens are folded into the state on the CUDA cores in
+//           fp32, split across the warps of a head.
+#pragma once
+
+#include "mg_common.cuh"
+
+namespace mg {
+
+constexpr int kWarps = 16;     // warps per CTA (one CTA per SM): <= 128 registers per thread
+constexpr int kWarpsWide = 8;  // head_dim 128 or two n-tiles with <= 8 kv heads: <= 255 registers
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 2^8 in fp16
+constexpr int kMetaLanes = 32;             // page ids / scales cached per warp (one per lane)
+
+struct DecodeParams {
+    const void* q;
+    int q_f16;
+    const uint8_t* k_pool;
+    const uint8_t* v_pool;
+    const float* k_scales;
+    const float* v_scales;
+    const void* staging_k;
+    const void* staging_v;
+    int st_f16;
+    int has_staging;
+    const int32_t* block_tables;
+    int32_t max_blocks;
+    const int32_t* seq_lens;
+    int32_t uniform_len;  // >= 0: every sequence has this many committed tokens (legacy op)
+    int batch;
+    int Hq, Hkv, G, P;
+    FastDiv pdiv;
+    int page_bytes;
+    int nconsumers;    // warps per CTA
+    int wph;           // warps per kv head
+    int st_row_bytes;  // bytes of one staged token row (Hkv * D * element size)
+    int scratch_off;   // dynamic shared memory: softmax-state merge scratch (wph > 1)
+    int tail_off;      // dynamic shared memory: staged-tail buffer
+    int tail_cap;      // its size in bytes (0: tails are read from global memory)
+    float sm_scale_log2;
+    int64_t num_pages;
+    void* out;
+    int out_f16;
+    float* out_wv;  // unnormalised outputs (legacy op) when non-null
+    float* out_l;
+    float* out_m;
+    float* ws_acc;  // [2*G, Hq, HD]
+    float* ws_m;    // [2*G, Hq]
+    float* ws_l;    // [2*G, Hq]
+    uint32_t* tickets;  // [batch]
+    int32_t* status;
+};
+
+struct DecodePlan {
+    int nt, split_mode, hpw, wph, nconsumers, nwarps;
+    int grid;
+    int scratch_off, tail_off, tail_cap;
+    int64_t smem_bytes;
+    int64_t ws_bytes;
+};
+
+template <bool KV4, int HD, int NT>
+struct Cfg {
+    static constexpr int KSTEPS = HD / 16;
+    static constexpr int MTILES = HD / 16;
+    static constexpr int ROWB = KV4 ? HD / 2 : HD;  // bytes per (token, head) row
+    static constexpr int KCHB = ROWB / 4;           // K bytes per lane per row
+    static constexpr int VCHB = ROWB / 8;           // V bytes per lane per token
+    static constexpr int VE = HD / 8;               // d values per lane
+};
+
+// BYTES (4, 8, 16 or 32, naturally aligned) of page data per lane into
+// 32-bit words: streaming loads (read once per launch, evict first).
+template <int BYTES>
+__device__ __forceinline__ void ldg_words(const uint8_t* p, uint32_t (&w)[BYTES / 4]) {
+    if constexpr (BYTES == 4) {
+        w[0] = __ldcs(reinterpret_cast<const unsigned int*>(p));
+    } else if constexpr (BYTES == 8) {
+        const uint2 v = __ldcs(reinterpret_cast<const uint2*>(p));
+        w[0] = v.x;
+        w[1] = v.y;
+    } else if constexpr (BYTES == 16) {
+        const uint4 v = __ldcs(reinterpret_cast<const uint4*>(p));
+        w[0] = v.x;
+        w[1] = v.y;
+        w[2] = v.z;
+        w[3] = v.w;
+    } else {
+        static_assert(BYTES == 32, "row chunk");
+        const uint4 v = __ldcs(reinterpret_cast<const uint4*>(p));
+        const uint4 u = __ldcs(reinterpret_cast<const uint4*>(p + 16));
+        w[0] = v.x;
+        w[1] = v.y;
+        w[2] = v.z;
+        w[3] = v.w;
+        w[4] = u.x;
+        w[5] = u.y;
+        w[6] = u.z;
+        w[7] = u.w;
+    }
+}
+
+// d (within the head) held by K-fragment slot s (0: k=2c, 1: 2c+1, 2: 2c+8,
+// 3: 2c+9) of k-step kk for lane column c; must match k_frag_row().
+template <bool KV4, int HD>
+__device__ __forceinline__ int k_slot_d(int kk, int c, int s) {
+    if (!KV4) {
+        // word kk of the lane's chunk; a0 = bytes (0,2), a2 = bytes (1,3)
+        const int off = (s == 0) ? 0 : (s == 1) ? 2 : (s == 2) ? 1 : 3;
+        return (HD / 4) * c + 4 * kk + off;
+    } else {
+        // word kk>>1 (8 nibbles); h = kk&1 picks nibbles (2h,2h+4) and (2h+1,2h+5)
+        const int off = (s == 0) ? 0 : (s == 1) ? 4 : (s == 2) ? 1 : 5;
+        return (HD / 4) * c + 8 * (kk >> 1) + 2 * (kk & 1) + off;
+    }
+}
+
+template <bool KV4>
+__device__ __forceinline__ void k_frag_row(const uint32_t* w, int kk, uint32_t& lo, uint32_t& hi) {
+    if (!KV4) {
+        const uint32_t x = w[kk];
+        lo = s8pair_to_half2(x);       // bytes 0, 2
+        hi = s8pair_to_half2(x >> 8);  // bytes 1, 3
+    } else {
+        const uint32_t x = w[kk >> 1] ^ 0x88888888u;
+        const uint32_t y = (kk & 1) ? (x >> 8) : x;
+        lo = s4pair_lo_to_half2(y);  // nibbles (2h, 2h+4)
+        hi = s4pair_hi_to_half2(y);  // nibbles (2h+1, 2h+5)
+    }
+}
+
+// V A-fragment pairs for one token pair (A at k-slot 2c[+8], B at 2c+1[+9]):
+// for each m-tile mt, r0 = (A, B) codes at d = VE*g + 2mt, r1 at d + 1.
+template <bool KV4, int HD>
+__device__ __forceinline__ void v_pairs(const uint32_t* wa, const uint32_t* wb, uint32_t (&r0)[HD / 16],
+                                        uint32_t (&r1)[HD / 16]) {
+    if (!KV4) {
+#pragma unroll
+        for (int wi = 0; wi < HD / 32; ++wi) {
+            const uint32_t X = __byte_perm(wa[wi], wb[wi], 0x5410);  // A0 A1 B0 B1
+            const uint32_t Y = __byte_perm(wa[wi], wb[wi], 0x7632);  // A2 A3 B2 B3
+            r0[2 * wi] = s8pair_to_half2(X);
+            r1[2 * wi] = s8pair_to_half2(X >> 8);
+            r0[2 * wi + 1] = s8pair_to_half2(Y);
+            r1[2 * wi + 1] = s8pair_to_half2(Y >> 8);
+        }
+    } else {
+#pragma unroll
+        for (int wi = 0; wi < HD / 64; ++wi) {
+            const uint32_t X = __byte_perm(wa[wi], wb[wi], 0x5410) ^ 0x88888888u;
+            const uint32_t Y = __byte_perm(wa[wi], wb[wi], 0x7632) ^ 0x88888888u;
+            r0[4 * wi + 0] = s4pair_lo_to_half2(X);
+            r1[4 * wi + 0] = s4pair_hi_to_half2(X);
+            r0[4 * wi + 1] = s4pair_lo_to_half2(X >> 8);
+            r1[4 * wi + 1] = s4pair_hi_to_half2(X >> 8);
+            r0[4 * wi + 2] = s4pair_lo_to_half2(Y);
+            r1[4 * wi + 2] = s4pair_hi_to_half2(Y);
+            r0[4 * wi + 3] = s4pair_lo_to_half2(Y >> 8);
+            r1[4 * wi + 3] = s4pair_hi_to_half2(Y >> 8);
+        }
+    }
+}
+
+__device__ __forceinline__ float load_f(const void* p, int64_t i, int f16) {
+    return f16 ? __half2float(static_cast<const __half*>(p)[i]) : static_cast<const float*>(p)[i];
+}
+
+// Largest CTA index c in [0, G) whose unit range starts at or before u.
+__device__ __forceinline__ int cta_of_unit(int64_t u, int64_t W, int G) {
+    int lo = 0, hi = G - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if ((static_cast<int64_t>(mid) * W) / G <= u) lo = mid;
+        else hi = mid - 1;
+    }
+    return lo;
+}
+
+// Per-warp softmax state of one kv head: NT n-tiles x (SPLIT ? 1 : 2) columns.
+template <int NT, int MTILES>
+struct HeadState {
+    uint32_t qf[NT][MTILES][2];  // B fragments of q (MTILES == KSTEPS == HD/16)
+    float acc[MTILES][NT][4];
+    float m_used[NT][2];  // reference max used for the exponentials (log2 domain)
+    float m_true[NT][2];  // running true max
+    float lpart[NT][2];
+};
+
+// Register image of one 16-token tile of one kv head for lane (g, c): K rows
+// g and g+8 (KCHB bytes each, the lane's slice of the head dimension), V rows
+// 2c, 2c+1, 2c+8, 2c+9 (VCHB bytes each), and for rows g and g+8 the K scale
+// (times the softmax scale, log2 domain; 0 for a row past the end) and the V
+// scale of their pages.
+template <bool KV4, int HD>
+struct TileRegs {
+    static constexpr int KW = Cfg<KV4, HD, 1>::KCHB / 4;
+    static constexpr int VW = Cfg<KV4, HD, 1>::VCHB / 4;
+    uint32_t k[2][KW];
+    uint32_t v[4][VW];
+    float ks[2];
+    float vs[2];
+    uint32_t live;  // bit r: row g + 8r exists
+};
+
+// Page ids and scales of 32 upcoming pages of the warp's current segment,
+// lane i holding entry base + i (one shuffle per tile to read them).
+struct MetaCache {
+    int base;
+    int32_t pid;
+    float ks, vs;
+};
+
+template <bool KV4, int HD, int NT, bool SPLIT, bool P16, int HPW, int R, int NW>
+__global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodeParams p);
+
+mg_status make_decode_plan(int kv4, int hd, int P, int Hkv, int Hq, int q_f16, int batch, int staging_esize,
+                           DecodePlan* out);
+mg_status launch_decode_i8(const DecodeParams& p, const DecodePlan& pl, cudaStream_t s, int hd);
+mg_status launch_decode_i4(const DecodeParams& p, const DecodePlan& pl, cudaStream_t s, int hd);
+
+}  // namespace mg

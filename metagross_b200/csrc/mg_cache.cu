@@ -16,36 +16,6 @@ constexpr int kPlanThreads = 1024;
 constexpr int kAppendThreads = 256;
 constexpr int kGatherThreads = 256;
 
-// Block-wide exclusive scan of one int per thread; returns the exclusive
-// prefix, *total receives the block sum.  scratch >= 33 ints.
-__device__ int block_exclusive_scan(int v, int* scratch, int* total) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int nw = (blockDim.x + 31) >> 5;
-    int x = v;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        int y = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += y;
-    }
-    __syncthreads();
-    if (lane == 31) scratch[warp] = x;
-    __syncthreads();
-    if (warp == 0) {
-        int w = lane < nw ? scratch[lane] : 0;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            int y = __shfl_up_sync(0xffffffffu, w, o);
-            if (lane >= o) w += y;
-        }
-        if (lane < nw) scratch[lane] = w;  // inclusive per-warp offsets
-        if (lane == nw - 1) scratch[32] = w;
-    }
-    __syncthreads();
-    const int warp_off = warp == 0 ? 0 : scratch[warp - 1];
-    *total = scratch[32];
-    return warp_off + x - v;
-}
-
 __global__ void alloc_init_kernel(int32_t* free_stack, int32_t* n_free, int32_t* in_use, int64_t n) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         free_stack[i] = static_cast<int32_t>(i);

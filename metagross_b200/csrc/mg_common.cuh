@@ -70,6 +70,36 @@ __device__ __forceinline__ float block_max(float v, float* scratch) {
     return r;
 }
 
+// Block-wide exclusive scan of one int per thread; returns the exclusive
+// prefix, *total receives the block sum.  scratch >= 33 ints.
+__device__ __forceinline__ int block_exclusive_scan(int v, int* scratch, int* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nw = (blockDim.x + 31) >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    __syncthreads();
+    if (lane == 31) scratch[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < nw ? scratch[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            int y = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += y;
+        }
+        if (lane < nw) scratch[lane] = w;  // inclusive per-warp offsets
+        if (lane == nw - 1) scratch[32] = w;
+    }
+    __syncthreads();
+    const int warp_off = warp == 0 ? 0 : scratch[warp - 1];
+    *total = scratch[32];
+    return warp_off + x - v;
+}
+
 // ---------------------------------------------------------------------------
 // int8 / int4 -> fp16 conversion without I2F.
 // fp16 0x6400 is 1024.0 with a 10-bit mantissa of unit weight, so the half
@@ -194,6 +224,22 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, u
             smem_u32(dst_smem)),
         "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
+}
+
+// 16-byte asynchronous global -> shared copy (both addresses 16-byte aligned);
+// completion is awaited per thread with cp_async_wait_all().
+__device__ __forceinline__ void cp_async16(void* dst_smem, const void* src_gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(dst_smem)), "l"(src_gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
+// Programmatic dependent launch: block until the grids this one depends on
+// have completed (a no-op when launched without the attribute), and let the
+// next kernel in the stream start its launch early.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 }
 
 // Fast unsigned division by a runtime divisor d in [1, 2^16) for n < 2^16:
