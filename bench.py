@@ -8,6 +8,12 @@ allocator/planner launch, then per layer the KV append of one new token per
 sequence (a page commit every 16 steps) and the fused attention.  The 12
 pools (~610 MB) exceed the 126 MB L2, so no flush is needed between steps.
 
+The step runs as one CUDA graph (metagross_b200.DecodeGraph: begin_step, the
+step's decode plan, then per layer append + attention), so it is bound by the
+GPU rather than by per-kernel launch cost; sequence truncation stays an eager
+cache call.  The attention kernel's own time is measured on a graph of the 12
+attention launches alone (CUDA events around the replays).
+
 Each sequence's context stays within one page of its configured length: it
 grows one token per step and every 16 steps its last page is truncated back
 to the allocator (a real cache operation, counted in the timed region), so
@@ -50,6 +56,12 @@ WORKLOADS = {
     "tinyllama_int4": dict(batch=64, hq=32, hkv=4, d=64, page=16, ctx="uniform128_2048", layers=22, kv="int4",
                            desc="INT4 paged decode attention with GQA (32q/4kv), head_dim 64, block 16, batch 64, "
                                 "contexts U[128,2048], 22 layers, 1% outliers x8"),
+    # config: 1024 sequences sharded over the GPUs (strong scaling), log-normal contexts
+    "lognormal_int4": dict(batch=1024, hq=32, hkv=4, d=64, page=16, ctx="lognormal2048", layers=4, kv="int4",
+                           sharded=True,
+                           desc="INT4 paged decode attention, TinyLlama attention shape (32q/4kv, head_dim 64, "
+                                "block 16), 1024 sequences with contexts exp(N(ln 2048, 1.0)) capped at 32768, "
+                                "sharded over the GPUs by LPT on context length, 4 layers (pools > L2)"),
 }
 
 
@@ -176,6 +188,9 @@ def contexts_for(w, batch, seed):
     g = torch.Generator().manual_seed(seed)
     if w["ctx"] == "uniform128_2048":
         c = torch.randint(128, 2049, (batch,), generator=g)
+    elif w["ctx"] == "lognormal2048":
+        r = np.random.default_rng(seed)
+        c = torch.from_numpy(np.exp(r.normal(np.log(2048.0), 1.0, batch)).round().clip(1, 32768).astype(np.int64))
     else:
         c = torch.full((batch,), int(w["ctx"]))
     return c.to(torch.int32)
@@ -206,16 +221,18 @@ class Schedule:
         return ids, lens, self.cur.clone()
 
 
-def build(w, device, seed):
+def build(w, device, seed, ctx=None):
     from metagross_b200.batched import BatchedPagedKVCache
 
-    B, L, hkv, d, P, hq = w["batch"], w["layers"], w["hkv"], w["d"], w["page"], w["hq"]
-    ctx = contexts_for(w, B, seed)
+    L, hkv, d, P, hq = w["layers"], w["hkv"], w["d"], w["page"], w["hq"]
+    if ctx is None:
+        ctx = contexts_for(w, w["batch"], seed)
+    B = int(ctx.numel())
     start = ctx - 1
     max_final = int(ctx.max()) + P
     max_blocks = max_final // P + 2
     # pool with slack so physical pages come out of a shuffled free list
-    num_pages = B * max_blocks + 256
+    num_pages = int(((ctx.to(torch.int64) + 2 * P - 1) // P + 1).sum()) + 256
     cache = BatchedPagedKVCache(L, B, hkv, d, page_size=P, num_pages=num_pages, max_blocks=max_blocks,
                                 kv_dtype=w["kv"], staging_dtype=torch.float16, device=device)
     cache._workspace(hq, max_final)  # size the split workspace once, outside any timed region
@@ -224,17 +241,21 @@ def build(w, device, seed):
     perm = torch.randperm(num_pages, generator=g).to(torch.int32)
     cache.allocator.free_stack.copy_(perm.to(device))
     gd = torch.Generator(device=device).manual_seed(seed + 2)
-    # prefill every layer to the start contexts
-    cache.begin_step(start)
-    T = int(start.max())
-    for layer in range(L):
-        k = torch.randn(B, T, hkv, d, generator=gd, device=device, dtype=torch.float16)
-        v = torch.randn(B, T, hkv, d, generator=gd, device=device, dtype=torch.float16)
-        if w["kv"] == "int4":  # 1% outliers x8
-            k[torch.rand(k.shape, generator=gd, device=device) < 0.01] *= 8
-            v[torch.rand(v.shape, generator=gd, device=device) < 0.01] *= 8
-        cache.append(layer, k, v)
-        del k, v
+    # prefill every layer to the start contexts, in chunks of at most 512 tokens per sequence
+    done = torch.zeros_like(start)
+    while bool((done < start).any()):
+        n = torch.clamp(start - done, max=512)
+        T = int(n.max())
+        cache.begin_step(n)
+        for layer in range(L):
+            k = torch.randn(B, T, hkv, d, generator=gd, device=device, dtype=torch.float16)
+            v = torch.randn(B, T, hkv, d, generator=gd, device=device, dtype=torch.float16)
+            if w["kv"] == "int4":  # 1% outliers x8
+                k[torch.rand(k.shape, generator=gd, device=device) < 0.01] *= 8
+                v[torch.rand(v.shape, generator=gd, device=device) < 0.01] *= 8
+            cache.append(layer, k, v)
+            del k, v
+        done += n
     torch.cuda.synchronize()
     cache.check()
     cache._max_len = max_final
@@ -314,7 +335,7 @@ def traffic_per_launch(workload):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=30)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="gpt2_int8")
@@ -350,24 +371,54 @@ def main():
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
 
-    cache, sched, max_ctx, q, kn, vn, out = build(w, device, seed=1234 + rank)
-    L, B = w["layers"], w["batch"]
+    sharded = bool(w.get("sharded", False))
+    gatherer = None
     gather_buf = None
-    if world > 1:
-        gather_buf = torch.empty(world * B, w["hq"], w["d"], device=device, dtype=torch.float16)
+    if sharded:
+        # one global batch, split over the ranks by context length (strong scaling)
+        from metagross_b200.sharding import ShardGather, lpt_shard
+
+        glob_ctx = contexts_for(w, w["batch"], seed=1234)
+        shards = lpt_shard(glob_ctx.numpy(), world)
+        cache, sched, max_ctx, q, kn, vn, out = build(w, device, seed=1234 + rank,
+                                                      ctx=glob_ctx[torch.as_tensor(shards[rank])])
+        if world > 1:
+            gatherer = ShardGather(shards, rank, (w["hq"], w["d"]), torch.float16, device)
+    else:
+        # every rank runs the same per-GPU workload on its own sequences (weak scaling)
+        cache, sched, max_ctx, q, kn, vn, out = build(w, device, seed=1234 + rank)
+        if world > 1:
+            gather_buf = torch.empty(world * w["batch"], w["hq"], w["d"], device=device, dtype=torch.float16)
+    L, B = w["layers"], cache.batch
     e2e_steps = max(3, args.steps // 2)
     warm_plans = plan_steps(sched, args.warmup, device)
     timed_plans = plan_steps(sched, args.steps, device)
     e2e_plans = plan_steps(sched, e2e_steps, device)
 
-    def step(plan, ev=None, qq=q, kk=kn, vv=vn):
-        run_step(cache, qq, kk, vv, out, plan, max_ctx, ev)
+    from metagross_b200 import DecodeGraph
+
+    def gather():
         if world > 1:
             import torch.distributed as dist
 
-            dist.all_gather_into_tensor(gather_buf, out[L - 1])
+            if gatherer is not None:
+                gatherer(out[L - 1])
+            else:
+                dist.all_gather_into_tensor(gather_buf, out[L - 1])
 
-    for pl in warm_plans:
+    for pl in warm_plans[:2]:  # eager steps (allocate the workspace and plan buffers)
+        run_step(cache, q, kn, vn, out, pl, max_ctx)
+        gather()
+    graph = DecodeGraph(cache, q, kn, vn, out, n_new=1)
+
+    def step(plan):
+        ids, lens, _ = plan
+        if ids is not None:
+            cache.truncate(lens, ids)
+        graph.replay()
+        gather()
+
+    for pl in warm_plans[2:]:
         step(pl)
     torch.cuda.synchronize()
     cache.check()
@@ -382,8 +433,6 @@ def main():
     step_bytes = (att_b + app_b) / args.steps
     att_bytes_per_launch = att_b / (args.steps * L)
 
-    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
-          for _ in range(args.steps)]
     clocks = ClockSampler(local)
     clocks.start()
     if world > 1:
@@ -396,27 +445,50 @@ def main():
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record()
     for s in range(args.steps):
-        step(timed_plans[s], ev[s])
+        step(timed_plans[s])
     t1.record()
     torch.cuda.synchronize()
     clocks.mark_stop()
     clk = clocks.stop()
     ms = t0.elapsed_time(t1)
-    att_ms = [ev[s][l][0].elapsed_time(ev[s][l][1]) for s in range(args.steps) for l in range(L)]
-    att_avg_ms = sum(att_ms) / len(att_ms)
+    cache.check()
+
+    # ---- the attention kernel alone: a graph of the L attention launches ------------
+    cache._decode_plan()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    g_att = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(g_att, stream=side):
+            for layer in range(L):
+                cache.attend(layer, q[layer], out=out[layer], max_context=max_ctx)
+    torch.cuda.current_stream().wait_stream(side)
+    for _ in range(3):
+        g_att.replay()
+    att_reps = max(5, min(50, args.steps // 4))
+    a0 = torch.cuda.Event(enable_timing=True)
+    a1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a0.record()
+    for _ in range(att_reps):
+        g_att.replay()
+    a1.record()
+    torch.cuda.synchronize()
+    att_avg_ms = a0.elapsed_time(a1) / (att_reps * L)
+    att_lens = timed_plans[-1][2]
+    att_bytes_per_launch = attention_bytes(att_lens, w)
+    del g_att
     if world > 1:
         import torch.distributed as dist
 
         t = torch.tensor([ms, att_avg_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, att_avg_ms = float(t[0]), float(t[1])
-    cache.check()
 
     # ---- end to end through the public API with host buffers -----------------
     qh = q.cpu().pin_memory()
     knh, vnh = kn.cpu().pin_memory(), vn.cpu().pin_memory()
     outh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    qd, knd, vnd = torch.empty_like(q), torch.empty_like(kn), torch.empty_like(vn)
     e_bytes = 0.0
     for _, _, after in e2e_plans:
         e_bytes += L * (attention_bytes(after, w) + append_bytes(after, w))
@@ -429,10 +501,10 @@ def main():
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
     for s in range(e2e_steps):
-        qd.copy_(qh, non_blocking=True)
-        knd.copy_(knh, non_blocking=True)
-        vnd.copy_(vnh, non_blocking=True)
-        step(e2e_plans[s], None, qd, knd, vnd)
+        q.copy_(qh, non_blocking=True)  # the graph's input buffers, refilled from pinned host memory
+        kn.copy_(knh, non_blocking=True)
+        vn.copy_(vnh, non_blocking=True)
+        step(e2e_plans[s])
         outh.copy_(out, non_blocking=True)
     e1.record()
     torch.cuda.synchronize()
@@ -443,7 +515,15 @@ def main():
         t = torch.tensor([e_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e_ms = float(t[0])
-    e2e = {"value": round(world * e_bytes / (e_ms / 1e3) / 1e9, 1), "unit": "GB/s",
+    # whole-job totals: every rank's own bytes and sequences, summed
+    tot_step_bytes, tot_e_bytes, tot_batch = step_bytes, e_bytes, float(B)
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([step_bytes, e_bytes, float(B)], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        tot_step_bytes, tot_e_bytes, tot_batch = float(t[0]), float(t[1]), float(t[2])
+    e2e = {"value": round(tot_e_bytes / (e_ms / 1e3) / 1e9, 1), "unit": "GB/s",
            "h2d_bytes_per_step": int(q.numel() * 2 + kn.numel() * 2 + vn.numel() * 2),
            "d2h_bytes_per_step": int(out.numel() * 2), "ms_per_step": e_ms / e2e_steps}
     cache.check()
@@ -452,25 +532,28 @@ def main():
     if rank == 0:
         peak, peak_kind = peaks()
         achieved = att_bytes_per_launch / (att_avg_ms / 1e3) / 1e9
-        value = world * step_bytes / (ms / args.steps / 1e3) / 1e9
-        tok_s = world * B * args.steps / (ms / 1e3)
+        value = tot_step_bytes / (ms / args.steps / 1e3) / 1e9
+        tok_s = tot_batch * args.steps / (ms / 1e3)
         line = {
             "metric": metric, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong" if sharded else "weak",
             "vs_baseline": None, "dtype": w["kv"] if w["kv"] == "int8" else "int4", "data": "synthetic",
-            "config": {"workload": args.workload, "desc": w["desc"], "global_batch": world * B,
+            "config": {"workload": args.workload, "desc": w["desc"], "global_batch": int(tot_batch),
                        "context_mean": round(ctx_mean, 1), "truncations_timed": n_trunc,
                        "layers": L, "parallelism": f"sequence-sharded dp{world}",
                        "l2": "working set per step > 126 MB L2 (one pool per layer); no flush"},
             "decode_tokens_per_s": round(tok_s, 1),
-            "bytes_per_step": step_bytes * world,
+            "bytes_per_step": tot_step_bytes,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "traffic": traffic_per_launch(args.workload),
                          "kernel": "paged_decode_kernel", "algorithmic_bytes_per_launch": att_bytes_per_launch,
-                         "avg_launch_ms": att_avg_ms},
+                         "avg_launch_ms": att_avg_ms,
+                         "timing": f"graph of the {L} attention launches (one per layer pool), CUDA events, "
+                                   f"{att_reps} replays"},
             "e2e": e2e,
-            "gpu_launches": args.steps * (1 + 2 * L) + n_trunc,
+            "gpu_launches": args.steps * (2 + 2 * L) + n_trunc,
             "clocks": clk,
         }
         if world == 1 and not args.no_cpu_baseline:

@@ -197,13 +197,14 @@ MG_API mg_status mg_kv_append(const mg_cache_layout* layout, const mg_layer_ptrs
  * the block table plus the exact staged tail, one online softmax, split over
  * the context with an in-kernel merge.  q [batch, num_q_heads, D] (q_dtype),
  * out [batch, num_q_heads, D] (out_dtype) = softmax(scale * q K^T) V.
- * The work is split evenly over the GPU by pages (stream-K), so no length
- * bound is needed: max_context is accepted for compatibility and ignored.
+ * The work is split over the GPU by pages (see mg_paged_decode_plan, which
+ * this call runs first), so no length bound is needed: max_context is
+ * accepted for compatibility and ignored.
  * workspace: mg_paged_decode_workspace_bytes() bytes.  Its first
- * 256*ceil(4*batch/256) bytes are per-sequence merge counters that must be
- * zero before the first call; every call leaves them zero, so one zeroed
- * buffer can serve calls of any max_context and head count.  Calls that share
- * a workspace must not overlap on the device. */
+ * 256*ceil(4*batch*num_kv_heads/256) bytes are per-(sequence, kv head) merge
+ * counters that must be zero before the first call; every call leaves them
+ * zero, so one zeroed buffer can serve calls of any max_context and q-head
+ * count.  Calls that share a workspace must not overlap on the device. */
 MG_API mg_status mg_paged_decode_attention(const mg_cache_layout* layout, const mg_layer_ptrs* layer,
                                     const int32_t* block_tables, const int32_t* seq_lens,
                                     int32_t batch, const void* q, int32_t q_dtype,
@@ -212,6 +213,29 @@ MG_API mg_status mg_paged_decode_attention(const mg_cache_layout* layout, const 
                                     int32_t* dev_status, mg_stream_t stream);
 MG_API int64_t mg_paged_decode_workspace_bytes(const mg_cache_layout* layout, int32_t batch,
                                         int32_t num_q_heads, int32_t max_context);
+
+/* Decode plan: how one decode step's attention work is split over the GPU's
+ * SMs.  It depends only on seq_lens (and the page size), which every layer
+ * of a step shares, so a caller that runs attention for many layers builds
+ * it once per step (after the step's lengths change) and passes it to
+ * mg_paged_decode_attention_planned; mg_paged_decode_attention builds one
+ * inside its workspace on every call.  No counterpart in the reference (its
+ * paged_attention op handles one sequence per call, csrc/bindings.cpp:82-106).
+ * plan: mg_paged_decode_plan_bytes(batch) bytes, 16-byte aligned, device
+ * memory; with_staging says whether the attention calls will fold the staged
+ * tails in (it must match their staging pointers).  Invalid lengths set
+ * MG_DEV_BAD_ARGUMENT and are planned as empty. */
+MG_API int64_t mg_paged_decode_plan_bytes(int32_t batch);
+MG_API mg_status mg_paged_decode_plan(const mg_cache_layout* layout, const int32_t* seq_lens, int32_t batch,
+                               int32_t with_staging, void* plan, int64_t plan_bytes, int32_t* dev_status,
+                               mg_stream_t stream);
+/* mg_paged_decode_attention with a plan from mg_paged_decode_plan for the
+ * same batch and lengths; workspace as for mg_paged_decode_attention. */
+MG_API mg_status mg_paged_decode_attention_planned(const mg_cache_layout* layout, const mg_layer_ptrs* layer,
+                                            const int32_t* block_tables, const void* plan, int64_t plan_bytes,
+                                            int32_t batch, const void* q, int32_t q_dtype, int32_t num_q_heads,
+                                            float scale, void* out, int32_t out_dtype, void* workspace,
+                                            int64_t workspace_bytes, int32_t* dev_status, mg_stream_t stream);
 
 /* Standalone block gather + dequantize (the batched read_fp32 of
  * metagross/cache.py:74-85): for each sequence b, its committed pages in

@@ -23,12 +23,8 @@ def sanity_add(a, b):
 
 def __getattr__(name):
     # lazy re-exports, so importing the package never needs a GPU
-    if name in ("BatchedPagedKVCache",):
-        from .batched import BatchedPagedKVCache
+    if name in ("BatchedPagedKVCache", "DecodeGraph", "paged_decode_attention"):
+        from . import batched
 
-        return BatchedPagedKVCache
-    if name in ("paged_decode_attention",):
-        from .batched import paged_decode_attention
-
-        return paged_decode_attention
+        return getattr(batched, name)
     raise AttributeError(name)

@@ -21,6 +21,11 @@ A decode/prefill step is:
   cache.begin_step(n_new)              # allocate committing pages (once)
   for layer: cache.append(layer, k, v) # quantize filled pages, stage the rest
              out = cache.attend(layer, q)
+
+The first ``attend`` after the lengths change (begin_step, truncate, free,
+reset) builds the step's decode plan -- the split of the batch's pages over
+the SMs -- and the other layers reuse it.  Code that writes ``seq_lens``
+directly must call ``invalidate_plan()``.
 """
 from __future__ import annotations
 
@@ -86,6 +91,8 @@ class BatchedPagedKVCache:
         self._max_len = 0  # host-side upper bound on seq_lens
         self._ws = torch.zeros(0, dtype=torch.uint8, device=self.device)
         self._ws_key = None
+        self._plan = None
+        self._plan_ok = False
 
     # ------------------------------------------------------------------ steps
     def begin_step(self, n_new) -> None:
@@ -104,6 +111,7 @@ class BatchedPagedKVCache:
                 self._max_len = self.max_blocks * self.page_size + self.page_size - 1
             self.n_new.copy_(t.to(self.device), non_blocking=True)
         self._max_len = min(self._max_len, self.max_blocks * self.page_size + self.page_size - 1)
+        self._plan_ok = False
         C.plan_append(self.allocator.free_stack, self.allocator.n_free, self.allocator.in_use, self.block_tables,
                       self.seq_lens, self.n_new, self.page_size, self.status)
 
@@ -114,6 +122,20 @@ class BatchedPagedKVCache:
         _get_C().kv_append(self.k_pool[layer], self.v_pool[layer], self.k_scales[layer], self.v_scales[layer],
                            self.staging_k[layer], self.staging_v[layer], self.block_tables, self.seq_lens,
                            self.n_new, k_new, v_new, self.status)
+
+    def invalidate_plan(self) -> None:
+        """Mark the decode plan stale (after writing seq_lens directly)."""
+        self._plan_ok = False
+
+    def _decode_plan(self) -> torch.Tensor:
+        """The step's decode plan, rebuilt on the device when the lengths changed."""
+        C = _get_C()
+        if self._plan is None:
+            self._plan = torch.zeros(C.decode_plan_bytes(self.batch), dtype=torch.uint8, device=self.device)
+        if not self._plan_ok:
+            C.decode_plan(self.k_pool[0], self.block_tables, self.seq_lens, True, self._plan, self.status)
+            self._plan_ok = True
+        return self._plan
 
     def _workspace(self, num_q_heads: int, max_context: int) -> torch.Tensor:
         key = (num_q_heads, max_context)
@@ -139,9 +161,11 @@ class BatchedPagedKVCache:
         ws = self._workspace(hq, mc)
         if out is None:
             out = torch.empty_like(q)
-        _get_C().paged_decode_attention(q.contiguous(), self.k_pool[layer], self.v_pool[layer], self.k_scales[layer],
-                                        self.v_scales[layer], self.staging_k[layer], self.staging_v[layer],
-                                        self.block_tables, self.seq_lens, sc, mc, ws, out, self.status)
+        plan = self._decode_plan()
+        _get_C().paged_decode_attention_planned(q.contiguous(), self.k_pool[layer], self.v_pool[layer],
+                                                self.k_scales[layer], self.v_scales[layer], self.staging_k[layer],
+                                                self.staging_v[layer], self.block_tables, plan, sc, ws, out,
+                                                self.status)
         return out
 
     def gather(self, layer: int, dtype=torch.float32, include_staging: bool = True):
@@ -164,6 +188,7 @@ class BatchedPagedKVCache:
     def free(self, seq_ids) -> None:
         """Return every page of the given sequences to the pool and reset them to length 0."""
         ids = torch.as_tensor(seq_ids, dtype=torch.int32).to(self.device)
+        self._plan_ok = False
         _get_C().free_sequences(self.allocator.free_stack, self.allocator.n_free, self.allocator.in_use,
                                 self.block_tables, self.seq_lens, ids, self.page_size, self.status)
 
@@ -179,6 +204,7 @@ class BatchedPagedKVCache:
             nl = torch.full((ids.numel(),), new_lens, dtype=torch.int32)
         else:
             nl = torch.as_tensor(new_lens, dtype=torch.int32)
+        self._plan_ok = False
         _get_C().truncate_sequences(self.allocator.free_stack, self.allocator.n_free, self.allocator.in_use,
                                     self.block_tables, self.seq_lens, ids.to(self.device), nl.to(self.device),
                                     self.page_size, self.status)
@@ -189,6 +215,7 @@ class BatchedPagedKVCache:
         self.block_tables.zero_()
         self.status.zero_()
         self._max_len = 0
+        self._plan_ok = False
 
     # ------------------------------------------------------------- inspection
     def check(self) -> None:
@@ -200,6 +227,54 @@ class BatchedPagedKVCache:
 
     def memory_bytes(self) -> int:
         return self.k_pool.numel() + self.v_pool.numel()
+
+
+class DecodeGraph:
+    """One decode step over every layer of ``cache`` captured as a CUDA graph:
+    begin_step(n_new) (page allocation), the step's decode plan, then per layer
+    append(k_new[l], v_new[l]) and attend(q[l]) -> out[l], all on the fixed
+    device buffers given here.  ``replay()`` runs a step with one launch from
+    the host, so the step is bound by the GPU, not by per-kernel launch cost.
+    Refill q / k_new / v_new in place between replays; truncate / free stay
+    eager calls on the cache (they take a different set of sequences each time).
+
+    q [L, B, Hq, D], k_new / v_new [L, B, T, Hkv, D] (or [L, B, Hkv, D] for
+    T = 1), out [L, B, Hq, D]."""
+
+    def __init__(self, cache: BatchedPagedKVCache, q, k_new, v_new, out, n_new=1, scale=None):
+        if not isinstance(n_new, int) or n_new < 0:
+            raise ValueError("n_new must be a non-negative int")
+        L = cache.num_layers
+        for name, t in (("q", q), ("k_new", k_new), ("v_new", v_new), ("out", out)):
+            if t.device != cache.device or t.shape[0] != L:
+                raise ValueError(f"{name} must be a [{L}, ...] tensor on {cache.device}")
+        self.cache, self.q, self.k_new, self.v_new, self.out = cache, q, k_new, v_new, out
+        self.n_new, self.scale = n_new, scale
+        # buffers the step reuses must exist before capture
+        cache._workspace(q.shape[2], cache.max_blocks * cache.page_size)
+        cache._decode_plan()
+        stream = torch.cuda.Stream(cache.device)
+        stream.wait_stream(torch.cuda.current_stream(cache.device))
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(self.graph, stream=stream):
+                self._step()
+        torch.cuda.current_stream(cache.device).wait_stream(stream)
+        cache._plan_ok = False  # the capture ran nothing; the plan buffer holds the eager plan
+
+    def _step(self):
+        c = self.cache
+        c.begin_step(self.n_new)
+        for layer in range(c.num_layers):
+            c.append(layer, self.k_new[layer], self.v_new[layer])
+            c.attend(layer, self.q[layer], scale=self.scale, out=self.out[layer],
+                     max_context=c.max_blocks * c.page_size)
+
+    def replay(self) -> None:
+        self.graph.replay()
+        self.cache._max_len = min(self.cache._max_len + self.n_new,
+                                  self.cache.max_blocks * self.cache.page_size + self.cache.page_size - 1)
+        self.cache._plan_ok = False  # lengths moved on the device
 
 
 def paged_decode_attention(cache: BatchedPagedKVCache, layer: int, q: torch.Tensor, scale=None, out=None):

@@ -439,6 +439,59 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_pool, torch::Tensor
                  "paged_decode_attention");
 }
 
+int64_t decode_plan_bytes(int64_t batch) { return mg_paged_decode_plan_bytes(static_cast<int32_t>(batch)); }
+
+// Build the step's decode plan from seq_lens into `plan` (uint8 CUDA tensor of
+// decode_plan_bytes(batch) bytes).  k_pool / block_tables give the layout.
+void decode_plan(torch::Tensor k_pool, torch::Tensor block_tables, torch::Tensor seq_lens, bool with_staging,
+                 torch::Tensor plan, c10::optional<torch::Tensor> status) {
+    const c10::cuda::CUDAGuard guard(seq_lens.device());
+    TORCH_CHECK(k_pool.is_cuda() && k_pool.dim() == 4, "k_pool must be a 4-D CUDA tensor");
+    check_i32_vec(block_tables, 1, "block_tables");
+    TORCH_CHECK(block_tables.dim() == 2, "block_tables must be [batch, max_blocks]");
+    const int64_t B = block_tables.size(0);
+    check_i32_vec(seq_lens, B, "seq_lens");
+    TORCH_CHECK(plan.is_cuda() && plan.is_contiguous() && plan.scalar_type() == torch::kUInt8,
+                "plan must be a contiguous CUDA uint8 tensor");
+    mg_cache_layout L{};
+    const bool i4 = k_pool.scalar_type() == torch::kUInt8;
+    L.kv_dtype = i4 ? MG_KV_INT4 : MG_KV_INT8;
+    L.staging_dtype = MG_F16;
+    L.page_size = static_cast<int32_t>(k_pool.size(1));
+    L.num_kv_heads = static_cast<int32_t>(k_pool.size(2));
+    L.head_dim = static_cast<int32_t>(i4 ? k_pool.size(3) * 2 : k_pool.size(3));
+    L.max_blocks = static_cast<int32_t>(block_tables.size(1));
+    L.num_pages = k_pool.size(0);
+    check_status(mg_paged_decode_plan(&L, seq_lens.data_ptr<int32_t>(), static_cast<int32_t>(B), with_staging ? 1 : 0,
+                                      plan.data_ptr(), plan.numel(), status_ptr(status), cur_stream()),
+                 "decode_plan");
+}
+
+void paged_decode_attention_planned(torch::Tensor q, torch::Tensor k_pool, torch::Tensor v_pool,
+                                    torch::Tensor k_scales, torch::Tensor v_scales,
+                                    c10::optional<torch::Tensor> staging_k, c10::optional<torch::Tensor> staging_v,
+                                    torch::Tensor block_tables, torch::Tensor plan, double scale,
+                                    torch::Tensor workspace, torch::Tensor out, c10::optional<torch::Tensor> status) {
+    const c10::cuda::CUDAGuard guard(q.device());
+    auto p = make_pools(k_pool, v_pool, k_scales, v_scales, staging_k, staging_v, block_tables);
+    const int64_t B = block_tables.size(0);
+    TORCH_CHECK(q.is_cuda() && q.dim() == 3 && q.size(0) == B && q.size(2) == p.L.head_dim && q.is_contiguous(),
+                "q must be a contiguous CUDA tensor [batch, num_q_heads, head_dim]");
+    TORCH_CHECK(out.is_cuda() && out.sizes() == q.sizes() && out.is_contiguous(),
+                "out must be a contiguous CUDA tensor shaped like q");
+    TORCH_CHECK(std::isfinite(scale) && scale > 0.0, "attention scale must be positive and finite, got ", scale);
+    TORCH_CHECK(workspace.is_cuda() && workspace.is_contiguous(), "workspace must be a contiguous CUDA tensor");
+    TORCH_CHECK(plan.is_cuda() && plan.is_contiguous() && plan.scalar_type() == torch::kUInt8,
+                "plan must be a contiguous CUDA uint8 tensor");
+    check_status(mg_paged_decode_attention_planned(
+                     &p.L, &p.ptrs, block_tables.data_ptr<int32_t>(), plan.data_ptr(), plan.numel(),
+                     static_cast<int32_t>(B), q.data_ptr(), float_code(q, "q"), static_cast<int32_t>(q.size(1)),
+                     static_cast<float>(scale), out.data_ptr(), float_code(out, "out"),
+                     workspace.numel() > 0 ? workspace.data_ptr() : nullptr,
+                     workspace.numel() * workspace.element_size(), status_ptr(status), cur_stream()),
+                 "paged_decode_attention_planned");
+}
+
 void gather_dequant(torch::Tensor k_pool, torch::Tensor v_pool, torch::Tensor k_scales, torch::Tensor v_scales,
                     c10::optional<torch::Tensor> staging_k, c10::optional<torch::Tensor> staging_v,
                     torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor cu_seqlens, int64_t max_context,
@@ -498,6 +551,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           pybind11::arg("v_scales"), pybind11::arg("staging_k"), pybind11::arg("staging_v"),
           pybind11::arg("block_tables"), pybind11::arg("seq_lens"), pybind11::arg("scale"),
           pybind11::arg("max_context"), pybind11::arg("workspace"), pybind11::arg("out"),
+          pybind11::arg("status") = pybind11::none());
+    m.def("decode_plan_bytes", &decode_plan_bytes, "Bytes of a decode plan for a batch");
+    m.def("decode_plan", &decode_plan, "Build the step's decode plan (work split over the SMs) from seq_lens",
+          pybind11::arg("k_pool"), pybind11::arg("block_tables"), pybind11::arg("seq_lens"),
+          pybind11::arg("with_staging"), pybind11::arg("plan"), pybind11::arg("status") = pybind11::none());
+    m.def("paged_decode_attention_planned", &paged_decode_attention_planned,
+          "Fused batched paged decode attention with a prebuilt decode plan", pybind11::arg("q"),
+          pybind11::arg("k_pool"), pybind11::arg("v_pool"), pybind11::arg("k_scales"), pybind11::arg("v_scales"),
+          pybind11::arg("staging_k"), pybind11::arg("staging_v"), pybind11::arg("block_tables"), pybind11::arg("plan"),
+          pybind11::arg("scale"), pybind11::arg("workspace"), pybind11::arg("out"),
           pybind11::arg("status") = pybind11::none());
     m.def("gather_dequant", &gather_dequant, "Block-table gather + dequantize of whole sequences",
           pybind11::arg("k_pool"), pybind11::arg("v_pool"), pybind11::arg("k_scales"), pybind11::arg("v_scales"),

@@ -9,8 +9,8 @@ namespace {
 
 int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 
-constexpr int64_t kSmemBudget = 200 * 1024;  // prefix + merge scratch + staged tail, one CTA per SM
-constexpr int kMaxBatch = 8192;              // unit prefix lives in shared memory
+constexpr int64_t kSmemBudget = 220 * 1024;  // prefix + merge scratch + tail slots, one CTA per SM
+constexpr int kMaxBatch = 8192;              // the plan kernel keeps six ints per sequence in shared memory
 
 }  // namespace
 
@@ -33,11 +33,22 @@ mg_status make_decode_plan(int kv4, int hd, int P, int Hkv, int Hq, int q_f16, i
     }
     if (pl.nt > 2) return set_error(MG_ERR_UNSUPPORTED, "GQA group %d too large (fp32 q: <= 8, fp16 q: <= 16)", G);
     // warps: one kv head each, several warps per head when there are few kv
-    // heads, two heads per warp (head_dim 64, one n-tile) beyond that; the
-    // register-heavy shapes (head_dim 128, two n-tiles) run 8 wide warps when
-    // there are at most 8 kv heads
+    // heads, two heads per warp (head_dim 64, one n-tile) beyond that.  Head
+    // dim 64 with one n-tile picks 12 warps (deep ring) or 16 (more warps) by
+    // the bytes each SM keeps in flight; the register-heavy shapes (head_dim
+    // 128, two n-tiles) run 8 wide warps when there are at most 8 kv heads.
     const bool light = hd == 64 && pl.nt == 1;
-    pl.nwarps = (!light && Hkv <= kWarpsWide) ? kWarpsWide : kWarps;
+    const int tile_bytes = 16 * (kv4 ? hd / 2 : hd);
+    if (light && Hkv <= kWarps) {
+        auto in_flight = [&](int nw) -> int64_t {
+            if (Hkv > nw) return -1;
+            const int used = Hkv * (nw / Hkv);
+            return static_cast<int64_t>(used) * (decode_ring(kv4 != 0, hd, pl.nt, 1, nw) - 1) * tile_bytes;
+        };
+        pl.nwarps = in_flight(kWarpsDeep) >= in_flight(kWarps) ? kWarpsDeep : kWarps;
+    } else {
+        pl.nwarps = (!light && Hkv <= kWarpsWide) ? kWarpsWide : kWarps;
+    }
     if (Hkv <= pl.nwarps) {
         pl.hpw = 1;
         pl.wph = pl.nwarps / Hkv;
@@ -50,22 +61,33 @@ mg_status make_decode_plan(int kv4, int hd, int P, int Hkv, int Hq, int q_f16, i
         return set_error(MG_ERR_UNSUPPORTED, "num_kv_heads %d with head_dim %d and group %d not supported", Hkv, hd,
                          G);
     }
-    // dynamic shared memory: [unit prefix][merge scratch][staged tail K, V]
-    const int64_t prefix_bytes = align_up(static_cast<int64_t>(batch + 1) * 4, 128);
+    pl.ring = decode_ring(kv4 != 0, hd, pl.nt, pl.hpw, pl.nwarps);
+    // dynamic shared memory: [the CTA's plan records][head merge scratch][tail slots: warps x ring]
+    pl.grid = sm_count();
+    const PlanLayout lay = plan_layout(batch, pl.grid);
+    (void)lay;
+    const int64_t prefix_bytes = align_up(static_cast<int64_t>(kRecCache) * 32, 128);
+    const int ncols = pl.split_mode ? 1 : 2;
     const int64_t scratch_bytes =
-        pl.wph > 1 ? align_up(static_cast<int64_t>(pl.nconsumers) * 4 * (hd + 2) * 4, 128) : 0;
-    const int64_t tail_want = 2LL * (P - 1) * Hkv * hd * (staging_esize > 0 ? staging_esize : 0);
-    int64_t tail_cap = kSmemBudget - prefix_bytes - scratch_bytes;
-    if (tail_cap > tail_want) tail_cap = tail_want;
-    if (tail_cap < 0) tail_cap = 0;
-    tail_cap &= ~static_cast<int64_t>(127);
-    MG_REQUIRE(prefix_bytes + scratch_bytes <= kSmemBudget, "batch %d too large for the unit prefix", batch);
+        pl.wph > 1 ? align_up(static_cast<int64_t>(pl.nconsumers) * pl.nt * ncols * 4 * (hd + 2) * 4, 128) : 0;
+    int64_t slot = 0;
+    if (staging_esize > 0) {
+        const int64_t row = static_cast<int64_t>(hd) * staging_esize;  // one staged row of one head
+        slot = 2 * row > 2048 ? 2 * row : 2048;
+        // shrink to one row pair per slot when the batch needs the room
+        if (prefix_bytes + scratch_bytes + slot * pl.ring * pl.nconsumers > kSmemBudget) slot = 2 * row;
+    }
+    const int64_t tail_bytes = slot * pl.ring * pl.nconsumers;
+    MG_REQUIRE(prefix_bytes + scratch_bytes + tail_bytes <= kSmemBudget,
+               "batch %d too large for the shared-memory plan", batch);
     pl.scratch_off = static_cast<int>(prefix_bytes);
     pl.tail_off = static_cast<int>(prefix_bytes + scratch_bytes);
-    pl.tail_cap = static_cast<int>(tail_cap);
-    pl.smem_bytes = prefix_bytes + scratch_bytes + tail_cap;
-    pl.grid = sm_count();
-    pl.ws_bytes = align_up(static_cast<int64_t>(batch) * 4, 256) + 2LL * pl.grid * Hq * (hd + 2) * 4;
+    pl.tail_slot = static_cast<int>(slot);
+    pl.smem_bytes = prefix_bytes + scratch_bytes + tail_bytes;
+    // workspace: [tickets][partials: 2G slots][plan (used by the unplanned entry point)]
+    pl.partials_off = align_up(static_cast<int64_t>(batch) * Hkv * 4, 256);
+    pl.plan_off = align_up(pl.partials_off + 2LL * pl.grid * Hq * (hd + 2) * 4, 256);
+    pl.ws_bytes = pl.plan_off + lay.words * 4;
     *out = pl;
     return MG_OK;
 }
@@ -85,16 +107,17 @@ void fill_common(DecodeParams& p, const DecodePlan& pl, int P, int Hkv, int Hq, 
     p.wph = pl.wph;
     p.scratch_off = pl.scratch_off;
     p.tail_off = pl.tail_off;
-    p.tail_cap = pl.tail_cap;
+    p.tail_slot = pl.tail_slot;
     p.st_row_bytes = Hkv * hd * 4;  // replaced with the staging dtype's size where there is staging
+    p.lay = plan_layout(batch, pl.grid);
     p.sm_scale_log2 = static_cast<float>(scale * 1.4426950408889634);
     p.num_pages = num_pages;
 }
 
-// workspace: [tickets: batch u32, 256-aligned][acc: 2G x Hq x HD][m: 2G x Hq][l: 2G x Hq]
-void set_workspace(DecodeParams& p, const DecodePlan& pl, int batch, int Hq, int hd, void* ws) {
+// workspace: [tickets: batch x Hkv u32][acc: 2G x Hq x HD][m: 2G x Hq][l: 2G x Hq][plan]
+void set_workspace(DecodeParams& p, const DecodePlan& pl, int Hq, int hd, void* ws) {
     p.tickets = static_cast<uint32_t*>(ws);
-    float* f = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + align_up(static_cast<int64_t>(batch) * 4, 256));
+    float* f = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + pl.partials_off);
     const int64_t n = 2LL * pl.grid * Hq;
     p.ws_acc = f;
     p.ws_m = f + n * hd;
@@ -160,14 +183,18 @@ extern "C" mg_status mg_paged_attention_committed(const float* query, const int8
     p.has_staging = 0;
     p.block_tables = block_table;
     p.max_blocks = static_cast<int32_t>(num_blocks > 0 ? num_blocks : 1);
-    p.seq_lens = nullptr;
-    p.uniform_len = static_cast<int32_t>(num_blocks * page_size);
     p.out = nullptr;
     p.out_wv = out_wv;
     p.out_l = out_sum;
     p.out_m = out_max;
     p.status = dev_status;
-    set_workspace(p, pl, 1, static_cast<int>(num_q_heads), static_cast<int>(head_dim), workspace);
+    set_workspace(p, pl, static_cast<int>(num_q_heads), static_cast<int>(head_dim), workspace);
+    // one sequence of num_blocks committed pages: plan it, then attend
+    int32_t* plan = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + pl.plan_off);
+    st = launch_decode_plan(nullptr, static_cast<int32_t>(num_blocks * page_size), 1, static_cast<int>(page_size),
+                            p.max_blocks, 0, plan, pl.ws_bytes - pl.plan_off, dev_status, as_stream(stream));
+    if (st != MG_OK) return st;
+    p.plan = plan;
     return launch(0, static_cast<int>(head_dim), p, pl, as_stream(stream));
 }
 
@@ -182,30 +209,29 @@ extern "C" int64_t mg_paged_decode_workspace_bytes(const mg_cache_layout* L, int
     return pl.ws_bytes;  // independent of the query dtype and of max_context
 }
 
-extern "C" mg_status mg_paged_decode_attention(const mg_cache_layout* L, const mg_layer_ptrs* lp,
-                                               const int32_t* block_tables, const int32_t* seq_lens, int32_t batch,
-                                               const void* q, int32_t q_dtype, int32_t num_q_heads, float scale,
-                                               void* out, int32_t out_dtype, int32_t max_context, void* workspace,
-                                               int64_t workspace_bytes, int32_t* dev_status, mg_stream_t stream) {
+namespace {
+
+// Checks and kernel parameters shared by the planned and unplanned batched entry points.
+mg_status prepare_batched(const mg_cache_layout* L, const mg_layer_ptrs* lp, const int32_t* block_tables, int32_t batch,
+                          const void* q, int32_t q_dtype, int32_t num_q_heads, float scale, void* out,
+                          int32_t out_dtype, void* workspace, int64_t workspace_bytes, int32_t* dev_status,
+                          DecodeParams* pp, DecodePlan* plp) {
     mg_status st = check_cache_layout(L);
     if (st != MG_OK) return st;
     MG_REQUIRE(lp && lp->k_pool && lp->v_pool && lp->k_scales && lp->v_scales, "null layer pointer");
-    MG_REQUIRE(batch >= 0, "batch must be >= 0");
-    if (batch == 0) return MG_OK;
-    MG_REQUIRE(q && out && block_tables && seq_lens, "null pointer");
+    MG_REQUIRE(q && out && block_tables, "null pointer");
     MG_REQUIRE(q_dtype == MG_F32 || q_dtype == MG_F16, "q_dtype must be MG_F32 or MG_F16");
     MG_REQUIRE(out_dtype == MG_F32 || out_dtype == MG_F16, "out_dtype must be MG_F32 or MG_F16");
     MG_REQUIRE(scale > 0.0f && scale < 1.0f / 0.0f, "attention scale must be positive and finite");
     MG_REQUIRE(aligned16(lp->k_pool) && aligned16(lp->v_pool), "pools must be 16-byte aligned");
     MG_REQUIRE(aligned16(out), "out must be 16-byte aligned");
-    DecodePlan pl;
-    (void)max_context;
     const bool staged = lp->staging_k && lp->staging_v;
+    DecodePlan pl;
     st = make_decode_plan(L->kv_dtype == MG_KV_INT4, L->head_dim, L->page_size, L->num_kv_heads, num_q_heads,
                           q_dtype == MG_F16, batch, staged ? (L->staging_dtype == MG_F16 ? 2 : 4) : 0, &pl);
     if (st != MG_OK) return st;
-    MG_REQUIRE(workspace && workspace_bytes >= pl.ws_bytes, "workspace too small: %lld < %lld bytes",
-               (long long)workspace_bytes, (long long)pl.ws_bytes);
+    MG_REQUIRE(workspace && workspace_bytes >= pl.plan_off, "workspace too small: %lld < %lld bytes",
+               (long long)workspace_bytes, (long long)pl.plan_off);
     DecodeParams p{};
     fill_common(p, pl, L->page_size, L->num_kv_heads, num_q_heads, L->head_dim, L->kv_dtype == MG_KV_INT4, scale,
                 L->num_pages, batch);
@@ -218,18 +244,78 @@ extern "C" mg_status mg_paged_decode_attention(const mg_cache_layout* L, const m
     p.staging_k = lp->staging_k;
     p.staging_v = lp->staging_v;
     p.st_f16 = L->staging_dtype == MG_F16;
-    p.has_staging = (lp->staging_k && lp->staging_v) ? 1 : 0;
+    p.has_staging = staged ? 1 : 0;
     p.st_row_bytes = L->num_kv_heads * L->head_dim * (p.st_f16 ? 2 : 4);
     MG_REQUIRE(!p.has_staging || (aligned16(lp->staging_k) && aligned16(lp->staging_v)),
                "staging buffers must be 16-byte aligned");
     p.block_tables = block_tables;
     p.max_blocks = L->max_blocks;
-    p.seq_lens = seq_lens;
-    p.uniform_len = -1;
     p.out = out;
     p.out_f16 = out_dtype == MG_F16;
     p.out_wv = nullptr;
     p.status = dev_status;
-    set_workspace(p, pl, batch, num_q_heads, L->head_dim, workspace);
+    set_workspace(p, pl, num_q_heads, L->head_dim, workspace);
+    *pp = p;
+    *plp = pl;
+    return MG_OK;
+}
+
+}  // namespace
+
+extern "C" int64_t mg_paged_decode_plan_bytes(int32_t batch) {
+    if (batch < 1 || batch > kMaxBatch) return 0;
+    return plan_layout(batch, sm_count()).words * 4;
+}
+
+extern "C" mg_status mg_paged_decode_plan(const mg_cache_layout* L, const int32_t* seq_lens, int32_t batch,
+                                          int32_t with_staging, void* plan, int64_t plan_bytes, int32_t* dev_status,
+                                          mg_stream_t stream) {
+    mg_status st = check_cache_layout(L);
+    if (st != MG_OK) return st;
+    MG_REQUIRE(batch >= 1 && batch <= kMaxBatch, "batch must be in [1, %d], got %d", kMaxBatch, batch);
+    MG_REQUIRE(seq_lens, "null pointer");
+    return launch_decode_plan(seq_lens, -1, batch, L->page_size, L->max_blocks, with_staging ? 1 : 0,
+                              static_cast<int32_t*>(plan), plan_bytes, dev_status, as_stream(stream));
+}
+
+extern "C" mg_status mg_paged_decode_attention_planned(const mg_cache_layout* L, const mg_layer_ptrs* lp,
+                                                       const int32_t* block_tables, const void* plan,
+                                                       int64_t plan_bytes, int32_t batch, const void* q,
+                                                       int32_t q_dtype, int32_t num_q_heads, float scale, void* out,
+                                                       int32_t out_dtype, void* workspace, int64_t workspace_bytes,
+                                                       int32_t* dev_status, mg_stream_t stream) {
+    MG_REQUIRE(batch >= 0, "batch must be >= 0");
+    if (batch == 0) return MG_OK;
+    DecodeParams p;
+    DecodePlan pl;
+    mg_status st = prepare_batched(L, lp, block_tables, batch, q, q_dtype, num_q_heads, scale, out, out_dtype,
+                                   workspace, workspace_bytes, dev_status, &p, &pl);
+    if (st != MG_OK) return st;
+    MG_REQUIRE(plan && aligned16(plan) && plan_bytes >= p.lay.words * 4, "decode plan missing, unaligned or too small");
+    p.plan = static_cast<const int32_t*>(plan);
+    return launch(L->kv_dtype == MG_KV_INT4, L->head_dim, p, pl, as_stream(stream));
+}
+
+extern "C" mg_status mg_paged_decode_attention(const mg_cache_layout* L, const mg_layer_ptrs* lp,
+                                               const int32_t* block_tables, const int32_t* seq_lens, int32_t batch,
+                                               const void* q, int32_t q_dtype, int32_t num_q_heads, float scale,
+                                               void* out, int32_t out_dtype, int32_t max_context, void* workspace,
+                                               int64_t workspace_bytes, int32_t* dev_status, mg_stream_t stream) {
+    (void)max_context;
+    MG_REQUIRE(batch >= 0, "batch must be >= 0");
+    if (batch == 0) return MG_OK;
+    MG_REQUIRE(seq_lens, "null pointer");
+    DecodeParams p;
+    DecodePlan pl;
+    mg_status st = prepare_batched(L, lp, block_tables, batch, q, q_dtype, num_q_heads, scale, out, out_dtype,
+                                   workspace, workspace_bytes, dev_status, &p, &pl);
+    if (st != MG_OK) return st;
+    MG_REQUIRE(workspace_bytes >= pl.ws_bytes, "workspace too small: %lld < %lld bytes", (long long)workspace_bytes,
+               (long long)pl.ws_bytes);
+    int32_t* plan = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + pl.plan_off);
+    st = launch_decode_plan(seq_lens, -1, batch, L->page_size, L->max_blocks, p.has_staging, plan,
+                            pl.ws_bytes - pl.plan_off, dev_status, as_stream(stream));
+    if (st != MG_OK) return st;
+    p.plan = plan;
     return launch(L->kv_dtype == MG_KV_INT4, L->head_dim, p, pl, as_stream(stream));
 }

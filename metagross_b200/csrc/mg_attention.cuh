@@ -12,20 +12,26 @@
 //           gets a partial (m, l, acc) from each covering CTA; the last of
 //           them to finish (atomic ticket, no waiting) merges and writes the
 //           output.  Each CTA writes at most two partials (its first and its
-//           last sequence), so the workspace is O(G), not O(batch).
+//           last sequence), so the workspace is O(G), not O(batch); the
+//           tickets are per (sequence, kv head).
 //   data    no staging through shared memory for the pages: every warp loads
 //           its own 16-token tiles (one kv head's rows of K and V) straight
 //           from HBM into the registers in the tensor-core fragment layout,
 //           one (INT8) or two (INT4) tiles ahead of the math, so 16 warps per
 //           SM keep 32-64 KB of page data in flight.  The page ids and scales
 //           of a warp's next 32 tiles sit one per lane and travel by shuffle.
-//           A sequence's staged tail (< P exact fp16/fp32 rows, all heads) is
-//           copied to shared memory with cp.async when its segment starts and
-//           is folded in after the pages.
+//           A sequence's staged tail (< P exact fp16/fp32 rows) comes in
+//           chunks through a small per-warp shared-memory ring (cp.async) as
+//           further work items.  A warp walks all of its CTA's segments
+//           (sequences) as one stream of items, so the loads of the next
+//           segment are in flight while the current one is finalized.
 //   warps   each warp owns one kv head (two when there are more kv heads than
 //           warps); when the model has few kv heads, WPH warps share a head
-//           and take alternate tiles, merging their softmax states in shared
-//           memory at the end of a sequence.
+//           and take alternate tiles and tail rows, merging their softmax
+//           states in shared memory at the end of a sequence behind a named
+//           barrier of that head's warps only.  A sequence cut by CTA
+//           boundaries is merged per (sequence, kv head) by one warp of the
+//           last covering CTA, so no CTA-wide barrier follows the prologue.
 //   math    per 16-token tile, S^T = K Q^T and O^T += V^T P^T on the tensor
 //           cores (mma.sync m16n8k16, fp16 in, fp32 accumulate).  INT8/INT4
 //           codes are exact in fp16 and are converted in registers with the
@@ -36,17 +42,52 @@
 //           log2 domain with lazy rescaling (the running reference max moves
 //           only when a score exceeds it by 2^8).
 //   tail    the staged tokens are folded into the state on the CUDA cores in
-//           fp32, split across the warps of a head.
+//           fp32 (scores of a chunk, then its exponentials and V sums).
 #pragma once
 
 #include "mg_common.cuh"
 
 namespace mg {
 
-constexpr int kWarps = 16;     // warps per CTA (one CTA per SM): <= 128 registers per thread
-constexpr int kWarpsWide = 8;  // head_dim 128 or two n-tiles with <= 8 kv heads: <= 255 registers
+constexpr int kWarps = 16;      // warps per CTA (one CTA per SM): <= 128 registers per thread
+constexpr int kWarpsDeep = 12;  // head_dim 64, one n-tile: <= 168 registers, a deeper tile ring
+constexpr int kWarpsWide = 8;   // head_dim 128 or two n-tiles with <= 8 kv heads: <= 255 registers
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 2^8 in fp16
-constexpr int kMetaLanes = 32;             // page ids / scales cached per warp (one per lane)
+constexpr int kMetaLanes = 32;             // page ids cached per warp (one per lane)
+
+// Work items (tiles or staged-tail chunks) in flight per warp, by register
+// budget (R - 1 of them are loading while one is computed):
+//   head_dim 64, one n-tile, 12 warps (168 registers):      5 INT4, 4 INT8
+//   head_dim 64, one n-tile, 16 warps (128 registers):      4 INT4, 2 INT8,
+//                                                            2 with two kv heads per warp
+//   head_dim 128 or two n-tiles, 8 warps (255 registers):   2
+//   head_dim 128 or two n-tiles, 16 warps:                   1
+__host__ __device__ constexpr int decode_ring(bool kv4, int hd, int nt, int hpw, int nwarps) {
+    return (hd == 64 && nt == 1) ? (hpw == 2 ? 2 : nwarps == 12 ? (kv4 ? 5 : 4) : (kv4 ? 4 : 2))
+                                 : (nwarps == 8 ? 2 : 1);
+}
+
+// Decode plan buffer (int32 words), written once per step by the plan
+// kernel and read by every attention launch of the step:
+//   [0, 16)              header: magic, batch, grid, 0, n_empty, mode,
+//                        units, CTAs with work, has_staging
+//   [off_counts, +grid)  segments of each CTA
+//   [off_offs, +grid)    first record of each CTA in the flat array
+//   [off_recs, ...)      per CTA, its first kPlanInline records (one load)
+//   [off_flat, ...)      all records in CTA order, batch + grid at most
+//   [off_empty, +batch)  the sequences with nothing cached (outputs are zero)
+// A record is 8 words: {b, first page, pages, tail rows, partial slot (-1:
+// the whole sequence), first partial slot of b, pieces of b, 0}.
+constexpr int32_t kPlanMagic = 0x6d67706c;
+constexpr int kPlanInline = 4;    // records per CTA in the inline area
+constexpr int kRecCache = 64;     // records an attention CTA keeps in shared memory
+struct PlanLayout {
+    int off_counts, off_offs, off_recs, off_flat, off_empty;
+    int64_t words;
+};
+PlanLayout plan_layout(int batch, int grid);
+mg_status launch_decode_plan(const int32_t* seq_lens, int32_t uniform_len, int batch, int P, int max_blocks,
+                             int has_staging, int32_t* plan, int64_t plan_bytes, int32_t* status, cudaStream_t s);
 
 struct DecodeParams {
     const void* q;
@@ -61,8 +102,8 @@ struct DecodeParams {
     int has_staging;
     const int32_t* block_tables;
     int32_t max_blocks;
-    const int32_t* seq_lens;
-    int32_t uniform_len;  // >= 0: every sequence has this many committed tokens (legacy op)
+    const int32_t* plan;  // the step's decode plan (see PlanLayout)
+    PlanLayout lay;
     int batch;
     int Hq, Hkv, G, P;
     FastDiv pdiv;
@@ -71,8 +112,8 @@ struct DecodeParams {
     int wph;           // warps per kv head
     int st_row_bytes;  // bytes of one staged token row (Hkv * D * element size)
     int scratch_off;   // dynamic shared memory: softmax-state merge scratch (wph > 1)
-    int tail_off;      // dynamic shared memory: staged-tail buffer
-    int tail_cap;      // its size in bytes (0: tails are read from global memory)
+    int tail_off;      // dynamic shared memory: per-warp rings of staged-tail slots
+    int tail_slot;     // bytes of one slot
     float sm_scale_log2;
     int64_t num_pages;
     void* out;
@@ -90,7 +131,9 @@ struct DecodeParams {
 struct DecodePlan {
     int nt, split_mode, hpw, wph, nconsumers, nwarps;
     int grid;
-    int scratch_off, tail_off, tail_cap;
+    int ring;  // work items in flight per warp
+    int scratch_off, tail_off, tail_slot;
+    int64_t partials_off, plan_off;  // workspace offsets
     int64_t smem_bytes;
     int64_t ws_bytes;
 };

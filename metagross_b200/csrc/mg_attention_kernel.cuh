@@ -7,9 +7,10 @@
 namespace mg {
 
 // One 16-token tile of one kv head, already in registers: S^T = K Q^T on the
-// tensor cores, online softmax update, O^T += V^T P^T.
+// tensor cores, online softmax update, O^T += V^T P^T.  sscale: softmax scale
+// times log2(e).
 template <bool KV4, int HD, int NT, bool SPLIT>
-__device__ __forceinline__ void attend_tile(HeadState<NT, HD / 16>& S, const TileRegs<KV4, HD>& T) {
+__device__ __forceinline__ void attend_tile(HeadState<NT, HD / 16>& S, const TileRegs<KV4, HD>& T, float sscale) {
     using C = Cfg<KV4, HD, NT>;
     constexpr int NCOLS = SPLIT ? 1 : 2;
     const bool live0 = (T.live & 1u) != 0, live1 = (T.live & 2u) != 0;
@@ -31,7 +32,7 @@ __device__ __forceinline__ void attend_tile(HeadState<NT, HD / 16>& S, const Til
             else mma_16816(sc[nt], a, S.qf[nt][kk][0], S.qf[nt][kk][1]);
         }
     }
-    const float ks0 = T.ks[0], ks1 = T.ks[1];
+    const float ks0 = T.ks[0] * sscale, ks1 = T.ks[1] * sscale;
     const float vs0 = T.vs[0], vs1 = T.vs[1];
 
     // ---- online softmax (log2 domain, lazy rescale) ---------------------------------
@@ -191,15 +192,18 @@ __device__ __forceinline__ void load_row(const void* base, int64_t i, int f16, f
     }
 }
 
-// The exact staged tail: rows t0, t0 + ts, ... < tail of K at kbase and of V
-// at vbase (shared or global memory, layout [t][Hkv][D]), fp32 math on the
-// CUDA cores.
+// One chunk of the exact staged tail for one kv head: n rows of K at
+// kslot[i * HB] and of V at vslot[i * HB] (shared memory, HB = D * element
+// size), fp32 math on the CUDA cores in two passes (max, then exponentials
+// and the V accumulation) so the rows proceed independently.
 template <bool KV4, int HD, int NT, bool SPLIT>
-__device__ __forceinline__ void attend_tail(HeadState<NT, HD / 16>& S, const DecodeParams& p, const void* kbase,
-                                            const void* vbase, int b, int h, int t0, int ts, int tail, int g,
-                                            int c) {
+__device__ __forceinline__ void attend_tail_chunk(HeadState<NT, HD / 16>& S, const DecodeParams& p,
+                                                  const uint8_t* kslot, const uint8_t* vslot, int n, int b, int h,
+                                                  int g, int c) {
     constexpr int VE = HD / 8;
     constexpr int NCOLS = SPLIT ? 1 : 2;
+    const int esz = p.st_f16 ? 2 : 4;
+    const int hb = HD * esz;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -210,103 +214,141 @@ __device__ __forceinline__ void attend_tail(HeadState<NT, HD / 16>& S, const Dec
             float qv[VE];
 #pragma unroll
             for (int e = 0; e < VE; ++e) qv[e] = load_f(p.q, qrow + VE * g + e, p.q_f16);
-            for (int t = t0; t < tail; t += ts) {
-                const int64_t rel = (static_cast<int64_t>(t) * p.Hkv + h) * HD + VE * g;
-                float kv[VE], vv[VE];
-                load_row<VE>(kbase, rel, p.st_f16, kv);
-                load_row<VE>(vbase, rel, p.st_f16, vv);
+            auto score = [&](int i) -> float {
+                float kv[VE];
+                load_row<VE>(kslot + i * hb, VE * g, p.st_f16, kv);
                 float part = 0.0f;
 #pragma unroll
                 for (int e = 0; e < VE; ++e) part += qv[e] * kv[e];
                 part += __shfl_xor_sync(0xffffffffu, part, 4);
                 part += __shfl_xor_sync(0xffffffffu, part, 8);
                 part += __shfl_xor_sync(0xffffffffu, part, 16);
-                const float sv = part * p.sm_scale_log2;
-                S.m_true[nt][col] = fmaxf(S.m_true[nt][col], sv);
-                const float m_new = fmaxf(S.m_used[nt][col], sv);
-                const float alpha = ex2(S.m_used[nt][col] - m_new);
-                const float pr = ex2(sv - m_new);
-                S.m_used[nt][col] = m_new;
-                S.lpart[nt][col] = S.lpart[nt][col] * alpha + (g == 0 ? pr : 0.0f);
+                return part * p.sm_scale_log2;
+            };
+            float mloc = -INFINITY;
+#pragma unroll 4
+            for (int i = 0; i < n; ++i) mloc = fmaxf(mloc, score(i));
+            const float m_new = fmaxf(S.m_used[nt][col], mloc);
+            const float alpha = (S.m_used[nt][col] == -INFINITY) ? 0.0f : ex2(S.m_used[nt][col] - m_new);
+            S.m_used[nt][col] = m_new;
+            S.m_true[nt][col] = fmaxf(S.m_true[nt][col], mloc);
+            S.lpart[nt][col] *= alpha;
 #pragma unroll
-                for (int mt = 0; mt < HD / 16; ++mt) {
-                    if (SPLIT) {
-                        S.acc[mt][nt][0] = S.acc[mt][nt][0] * alpha + pr * vv[2 * mt];
-                        S.acc[mt][nt][1] *= alpha;
-                        S.acc[mt][nt][2] = S.acc[mt][nt][2] * alpha + pr * vv[2 * mt + 1];
-                        S.acc[mt][nt][3] *= alpha;
-                    } else {
-                        S.acc[mt][nt][col] = S.acc[mt][nt][col] * alpha + pr * vv[2 * mt];
-                        S.acc[mt][nt][col + 2] = S.acc[mt][nt][col + 2] * alpha + pr * vv[2 * mt + 1];
-                    }
+            for (int mt = 0; mt < HD / 16; ++mt) {
+                if (SPLIT) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) S.acc[mt][nt][i] *= alpha;
+                } else {
+                    S.acc[mt][nt][col] *= alpha;
+                    S.acc[mt][nt][col + 2] *= alpha;
                 }
             }
+            float lsum = 0.0f;
+#pragma unroll 4
+            for (int i = 0; i < n; ++i) {
+                const float pr = ex2(score(i) - m_new);
+                lsum += pr;
+                float vv[VE];
+                load_row<VE>(vslot + i * hb, VE * g, p.st_f16, vv);
+#pragma unroll
+                for (int mt = 0; mt < HD / 16; ++mt) {
+                    const int a0 = SPLIT ? 0 : col, a2 = SPLIT ? 2 : col + 2;
+                    S.acc[mt][nt][a0] += pr * vv[2 * mt];
+                    S.acc[mt][nt][a2] += pr * vv[2 * mt + 1];
+                }
+            }
+            if (g == 0) S.lpart[nt][col] += lsum;
         }
 }
 
-// Length of sequence b, or 0 (and BAD_ARGUMENT) when it is negative or its
-// committed pages (len / P; the staged rows need no block-table entry) do not
-// fit the block table.
-__device__ __forceinline__ int valid_len(const DecodeParams& p, int b, bool report) {
-    if (p.uniform_len >= 0) return p.uniform_len;
-    const int len = p.seq_lens[b];
-    if (len >= 0 && len / p.P <= p.max_blocks) return len;
-    if (report) flag(p.status, MG_DEV_BAD_ARGUMENT);
-    return 0;
-}
-
-// The part of sequence b inside the CTA's unit range [u0, u1).
+// A piece of one sequence run by this CTA (one record of the decode plan),
+// and this warp's work items in it: its tiles (segment tiles wsub,
+// wsub + wph, ..., times the warp's heads), then its chunks of the staged
+// tail (rows wsub, wsub + wph, ..., up to tt rows per chunk, times the
+// warp's heads).
 struct Segment {
     int b;
     int lo;      // first committed page of the segment (sequence-relative)
     int npg;     // committed pages in the segment
     int tail;    // staged rows folded in here (0: none, or another CTA's)
-    int ub, ue;  // the sequence's unit range
+    int pslot;   // partial slot, -1 when the segment is the whole sequence
+    int pbase;   // first partial slot of the sequence's pieces
+    int ncov;    // pieces of the sequence
     bool complete;
+    int nh;      // the warp's heads (1, or 2 with two heads per warp)
+    int ntile;   // the warp's tile items
+    int ntt;     // the warp's tail rows (per head)
+    int nchunk;  // its tail chunks (per head)
+    int nitems;  // ntile + nchunk * nh
 };
 
-__device__ __forceinline__ Segment make_segment(const DecodeParams& p, const int* prefix, int b, int64_t u0,
-                                                int64_t u1) {
+__device__ __forceinline__ Segment make_segment(const int4* rec, int P, int wsub, int wph, int nh, int tt) {
     Segment s;
-    const int ub = prefix[b], ue = prefix[b + 1];
-    const int lo = static_cast<int>((u0 > ub ? u0 : ub) - ub);
-    const int hi = static_cast<int>((u1 < ue ? u1 : ue) - ub);
-    const int len = valid_len(p, b, false);
-    const int np_b = len / p.P;
-    const int tail_b = p.has_staging ? len - np_b * p.P : 0;
-    s.b = b;
-    s.lo = lo;
-    s.npg = (hi < np_b ? hi : np_b) - lo;
-    if (s.npg < 0) s.npg = 0;
-    s.tail = (tail_b > 0 && hi == ue - ub) ? tail_b : 0;
-    s.ub = ub;
-    s.ue = ue;
-    s.complete = lo == 0 && hi == ue - ub;
+    const int4 r0 = rec[0], r1 = rec[1];
+    s.b = r0.x;
+    s.lo = r0.y;
+    s.npg = r0.z;
+    s.tail = r0.w;
+    s.pslot = r1.x;
+    s.pbase = r1.y;
+    s.ncov = r1.z;
+    s.complete = s.pslot < 0;
+    s.nh = nh;
+    const int ntiles = P == 16 ? s.npg : (s.npg * P + 15) >> 4;
+    const int nloc = wsub < ntiles ? (ntiles - 1 - wsub) / wph + 1 : 0;
+    s.ntile = nloc * nh;
+    s.ntt = wsub < s.tail ? (s.tail - 1 - wsub) / wph + 1 : 0;
+    s.nchunk = (s.ntt + tt - 1) / tt;
+    s.nitems = s.ntile + s.nchunk * nh;
     return s;
 }
 
-// Refill the warp's page-metadata cache from entry `base`.  P16: entry i is
-// the warp's local tile base + i, i.e. segment page wsub + (base + i) * wph;
-// otherwise entry i is segment page base + i.
+// Page metadata of 32 upcoming tiles of the issuing walk, one entry per lane.
+// P16: entry i is the warp's local tile base + i, i.e. segment page
+// wsub + (base + i) * wph; otherwise entry i is segment page base + i.
+template <bool P16>
+__device__ __forceinline__ const int32_t* meta_row(const DecodeParams& p, const Segment& sg) {
+    return p.block_tables + static_cast<int64_t>(sg.b) * p.max_blocks + sg.lo;
+}
+
 template <bool P16>
 __device__ __forceinline__ void meta_refill(MetaCache& mc, const DecodeParams& p, const Segment& sg, int base,
                                             int wsub, int wph, int lane) {
+    const int32_t* row = meta_row<P16>(p, sg);
     const int sp = P16 ? wsub + (base + lane) * wph : base + lane;
     int32_t pid = 0;
-    float ks = 0.0f, vs = 0.0f;
     if (sp < sg.npg) {
-        pid = p.block_tables[static_cast<int64_t>(sg.b) * p.max_blocks + sg.lo + sp];
+        pid = row[sp];
         if (pid < 0 || pid >= p.num_pages) {
             flag(p.status, MG_DEV_BAD_PAGE_ID);
             pid = 0;
         }
-        ks = p.k_scales[pid] * p.sm_scale_log2;
-        vs = p.v_scales[pid];
     }
     mc.base = base;
     mc.pid = pid;
-    mc.ks = ks;
-    mc.vs = vs;
+    // warm L1 with the next 32 entries (their lines) so the following refill does not wait on HBM
+    const int spn = P16 ? wsub + (base + kMetaLanes + lane) * wph : base + kMetaLanes + lane;
+    if (spn < sg.npg && (lane == 0 || P16)) prefetch_l1(row + spn);
+}
+
+// Warm L1 with a segment's first block-table entries and the q rows of the
+// warp's heads (issued when the walk enters the segment, read much later).
+template <bool P16>
+__device__ __forceinline__ void warm_segment(const DecodeParams& p, const Segment& sg, int h0, int h1, int HD,
+                                             int wsub, int wph, int lane) {
+    if (sg.nitems == 0) return;
+    const int32_t* row = meta_row<P16>(p, sg);
+    const int sp = P16 ? wsub + lane * wph : lane;
+    if (sp < sg.npg && (lane == 0 || P16)) prefetch_l1(row + sp);
+    const int qbytes = p.G * HD * (p.q_f16 ? 2 : 4);
+    const char* q0 = static_cast<const char*>(p.q) +
+                     (static_cast<int64_t>(sg.b) * p.Hq + static_cast<int64_t>(h0) * p.G) * HD * (p.q_f16 ? 2 : 4);
+    if (lane * 128 < qbytes) prefetch_l1(q0 + lane * 128);
+    if (h1 >= 0) {
+        const char* q1 = static_cast<const char*>(p.q) +
+                         (static_cast<int64_t>(sg.b) * p.Hq + static_cast<int64_t>(h1) * p.G) * HD * (p.q_f16 ? 2 : 4);
+        if (lane * 128 < qbytes) prefetch_l1(q1 + lane * 128);
+    }
 }
 
 // Issue the global loads of the warp's local tile jt (segment tile
@@ -319,10 +361,9 @@ __device__ __forceinline__ void load_tile(TileRegs<KV4, HD>& T, MetaCache& mc, c
     const int rs = p.Hkv * C::ROWB;  // bytes per token row of a page
     if (P16) {
         if (jt >= mc.base + kMetaLanes) meta_refill<true>(mc, p, sg, jt, wsub, wph, lane);
-        const int i = jt - mc.base;
-        const int32_t pid = __shfl_sync(0xffffffffu, mc.pid, i);
-        const float ks = __shfl_sync(0xffffffffu, mc.ks, i);
-        const float vs = __shfl_sync(0xffffffffu, mc.vs, i);
+        const int32_t pid = __shfl_sync(0xffffffffu, mc.pid, jt - mc.base);
+        const float ks = __ldg(p.k_scales + pid);
+        const float vs = __ldg(p.v_scales + pid);
         T.ks[0] = T.ks[1] = ks;
         T.vs[0] = T.vs[1] = vs;
         T.live = 3u;
@@ -353,13 +394,10 @@ __device__ __forceinline__ void load_tile(TileRegs<KV4, HD>& T, MetaCache& mc, c
             const bool live = x0 + row < ntok;
             const int rel = live ? off0 + row : 0;
             const int dp = static_cast<int>(p.pdiv.div(static_cast<uint32_t>(rel)));
-            const int src = pfirst + dp - mc.base;
             const int tok = rel - dp * P;
-            const int32_t pid = __shfl_sync(0xffffffffu, mc.pid, src);
-            const float ks = __shfl_sync(0xffffffffu, mc.ks, src);
-            const float vs = __shfl_sync(0xffffffffu, mc.vs, src);
-            T.ks[r] = live ? ks : 0.0f;
-            T.vs[r] = vs;
+            const int32_t pid = __shfl_sync(0xffffffffu, mc.pid, pfirst + dp - mc.base);
+            T.ks[r] = __ldg(p.k_scales + pid);
+            T.vs[r] = __ldg(p.v_scales + pid);
             T.live |= live ? (1u << r) : 0u;
             ldg_words<C::KCHB>(p.k_pool + static_cast<int64_t>(pid) * p.page_bytes + tok * rs + h * C::ROWB +
                                    c * C::KCHB,
@@ -370,14 +408,125 @@ __device__ __forceinline__ void load_tile(TileRegs<KV4, HD>& T, MetaCache& mc, c
             const int row = 2 * c + (r & 1) + (r >> 1) * 8;
             const int rel = x0 + row < ntok ? off0 + row : 0;
             const int dp = static_cast<int>(p.pdiv.div(static_cast<uint32_t>(rel)));
-            const int src = pfirst + dp - mc.base;
             const int tok = rel - dp * P;
-            const int32_t pid = __shfl_sync(0xffffffffu, mc.pid, src);
+            const int32_t pid = __shfl_sync(0xffffffffu, mc.pid, pfirst + dp - mc.base);
             ldg_words<C::VCHB>(p.v_pool + static_cast<int64_t>(pid) * p.page_bytes + tok * rs + h * C::ROWB +
                                    g * C::VCHB,
                                T.v[r]);
         }
     }
+}
+
+// cp.async the warp's tail rows wsub + wph * (chunk * tt + i), i < n, of kv
+// head h of sequence b into a shared slot: K rows [tt][HB], then V rows.
+__device__ __forceinline__ void issue_tail_chunk(uint8_t* slot, const DecodeParams& p, int b, int h, int chunk,
+                                                 int n, int tt, int hb, int wsub, int wph, int lane) {
+    const int pieces = hb / 16;  // 16-byte pieces per row
+    const int total = 2 * n * pieces;
+    const uint8_t* sk = static_cast<const uint8_t*>(p.staging_k);
+    const uint8_t* sv = static_cast<const uint8_t*>(p.staging_v);
+    for (int q = lane; q < total; q += 32) {
+        const int kv = q >= n * pieces;
+        const int r = kv ? q - n * pieces : q;
+        const int i = r / pieces, off = (r - i * pieces) * 16;
+        const int t = wsub + wph * (chunk * tt + i);
+        const int64_t src = ((static_cast<int64_t>(b) * p.P + t) * p.Hkv + h) * hb + off;
+        cp_async16(slot + (kv ? tt * hb : 0) + i * hb + off, (kv ? sv : sk) + src);
+    }
+}
+
+template <int N>
+struct Slot {
+    static constexpr int value = N;
+};
+
+// f(Slot<phase>{}) for a runtime phase in [K, R): the ring slot becomes a
+// compile-time index, so the register ring never spills to local memory.
+template <int R, int K = 0, typename F>
+__device__ __forceinline__ void with_slot(int phase, F&& f) {
+    if constexpr (K + 1 < R) {
+        if (phase == K) f(Slot<K>{});
+        else with_slot<R, K + 1>(phase, f);
+    } else {
+        f(Slot<K>{});
+    }
+}
+
+__device__ __forceinline__ uint32_t ticket_add(uint32_t* t) {
+    uint32_t prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(t) : "memory");
+    return prev;
+}
+
+// The last CTA to finish (sequence b, kv head h) merges the partials of all
+// pieces of the sequence (slots pbase .. pbase + ncov - 1; log-sum-exp, one
+// pass, four partials per load round) and writes the outputs of the head's
+// G query heads; one warp.
+template <int HD>
+__device__ __forceinline__ void merge_partials(const DecodeParams& p, int b, int h, int pbase, int ncov, int lane) {
+    constexpr float kLn2 = 0.6931471805599453f;
+    const int Hq = p.Hq;
+    for (int it = lane; it < p.G * (HD / 4); it += 32) {
+        const int gq = it / (HD / 4), d4 = (it - gq * (HD / 4)) * 4;
+        const int hq = h * p.G + gq;
+        float M = -INFINITY, L = 0.0f;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int k0 = 0; k0 < ncov; k0 += 4) {
+            float mj[4], lj[4];
+            float4 vj[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                mj[u] = -INFINITY;
+                lj[u] = 0.0f;
+                vj[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (k0 + u < ncov) {
+                    const int64_t prow = static_cast<int64_t>(pbase + k0 + u) * Hq + hq;
+                    mj[u] = __ldcg(p.ws_m + prow);
+                    lj[u] = __ldcg(p.ws_l + prow);
+                    vj[u] = __ldcg(reinterpret_cast<const float4*>(p.ws_acc + prow * HD + d4));
+                }
+            }
+            float Mn = M;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) Mn = fmaxf(Mn, mj[u]);
+            const float fo = (M == -INFINITY) ? 0.0f : ex2(M - Mn);
+            L *= fo;
+            a.x *= fo;
+            a.y *= fo;
+            a.z *= fo;
+            a.w *= fo;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float fj = (mj[u] == -INFINITY) ? 0.0f : ex2(mj[u] - Mn);
+                L += lj[u] * fj;
+                a.x += vj[u].x * fj;
+                a.y += vj[u].y * fj;
+                a.z += vj[u].z * fj;
+                a.w += vj[u].w * fj;
+            }
+            M = Mn;
+        }
+        const int64_t orow = static_cast<int64_t>(b) * Hq + hq;
+        const int64_t base_o = orow * HD + d4;
+        if (p.out_wv) {
+            *reinterpret_cast<float4*>(p.out_wv + base_o) = a;
+            if (d4 == 0) {
+                p.out_l[orow] = L;
+                p.out_m[orow] = M * kLn2;
+            }
+        } else {
+            const float inv = 1.0f / L;
+            if (p.out_f16) {
+                __half2* op = reinterpret_cast<__half2*>(static_cast<__half*>(p.out) + base_o);
+                op[0] = __floats2half2_rn(a.x * inv, a.y * inv);
+                op[1] = __floats2half2_rn(a.z * inv, a.w * inv);
+            } else {
+                *reinterpret_cast<float4*>(static_cast<float*>(p.out) + base_o) =
+                    make_float4(a.x * inv, a.y * inv, a.z * inv, a.w * inv);
+            }
+        }
+    }
+    if (lane == 0) p.tickets[static_cast<int64_t>(b) * p.Hkv + h] = 0u;  // leave the workspace reusable
 }
 
 template <bool KV4, int HD, int NT, bool SPLIT, bool P16, int HPW, int R, int NW>
@@ -386,155 +535,182 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
     constexpr int VE = C::VE;
     constexpr int NCOLS = SPLIT ? 1 : 2;
     constexpr float kLn2 = 0.6931471805599453f;
-    static_assert(HPW == 1 || R == 2, "two heads per warp alternate between two tile buffers");
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ int sm_scan[33];
-    __shared__ int sm_last;
+    __shared__ int sm_hdr[3];
 
     grid_dependency_wait();
     grid_launch_dependents();
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, c = lane & 3;
-    const int P = p.P, B = p.batch, Hkv = p.Hkv, Hq = p.Hq;
+    const int Hkv = p.Hkv, Hq = p.Hq;
     const int NCW = p.nconsumers, WPH = p.wph;
-    int* prefix = reinterpret_cast<int*>(smem);
+    const int cta = blockIdx.x;
     float* mscratch = reinterpret_cast<float*>(smem + p.scratch_off);
-    uint8_t* tailbuf = smem + p.tail_off;
+    uint8_t* tslots = smem + p.tail_off + static_cast<int64_t>(warp) * R * p.tail_slot;
+    int4* recs = reinterpret_cast<int4*>(smem);  // this CTA's segment records (plan)
 
     if (p.status && (*(volatile int32_t*)p.status & (MG_DEV_OUT_OF_PAGES | MG_DEV_BLOCK_TABLE_FULL))) return;
 
-    // ---- units per sequence (committed pages + 1 if a staged tail) and prefix ----
-    int base = 0;
-    for (int start = 0; start < B; start += blockDim.x) {
-        const int bb = start + tid;
-        int u = 0;
-        if (bb < B) {
-            const int len = valid_len(p, bb, blockIdx.x == 0);
-            const int np = len / P;
-            u = np + ((p.has_staging && len - np * P > 0) ? 1 : 0);
-        }
-        int tot;
-        const int ex = block_exclusive_scan(u, sm_scan, &tot);
-        if (bb < B) prefix[bb] = base + ex;
-        base += tot;
+    // ---- this CTA's segments from the step's plan: the first kPlanInline in one
+    // round trip, more (stream-K over many short sequences) from the flat array --
+    const int4* prec = reinterpret_cast<const int4*>(p.plan + p.lay.off_recs) + static_cast<int64_t>(cta) * kPlanInline * 2;
+    if (tid < 2 * kPlanInline) recs[tid] = __ldcg(prec + tid);
+    if (tid == 0) {
+        const bool ok = p.plan[0] == kPlanMagic && p.plan[1] == p.batch && p.plan[2] == static_cast<int>(gridDim.x) &&
+                        p.plan[8] == p.has_staging;
+        if (!ok) flag(p.status, MG_DEV_BAD_ARGUMENT);
+        sm_hdr[0] = ok ? p.plan[p.lay.off_counts + cta] : 0;
+        sm_hdr[1] = ok ? p.plan[4] : 0;
+        sm_hdr[2] = ok ? p.plan[p.lay.off_offs + cta] : 0;
     }
-    if (tid == 0) prefix[B] = base;
     __syncthreads();
-    const int64_t W = base;
-    const int cta = blockIdx.x;
-    const int GR = static_cast<int>(W < gridDim.x ? W : gridDim.x);
+    const int nseg = sm_hdr[0];
+    const int n_empty = sm_hdr[1];
+    const int4* flat = reinterpret_cast<const int4*>(p.plan + p.lay.off_flat) + static_cast<int64_t>(sm_hdr[2]) * 2;
+    if (nseg > kPlanInline) {
+        const int ncache = nseg < kRecCache ? nseg : kRecCache;
+        for (int i = 2 * kPlanInline + tid; i < 2 * ncache; i += blockDim.x) recs[i] = __ldcg(flat + i);
+        __syncthreads();
+    }
+    // record k: shared memory for the first kRecCache, the flat array beyond
+    auto rec = [&](int k) -> const int4* { return k < kRecCache ? recs + 2 * k : flat + 2 * k; };
 
     // empty sequences: zeros (normalised) or (0, 0, -inf) (unnormalised)
-    for (int bb = cta; bb < B; bb += gridDim.x) {
-        if (prefix[bb + 1] != prefix[bb]) continue;
+    for (int i = cta; i < n_empty; i += gridDim.x) {
+        const int bb = p.plan[p.lay.off_empty + i];
         const int64_t r0 = static_cast<int64_t>(bb) * Hq;
-        for (int i = tid; i < Hq * HD; i += blockDim.x) {
-            if (p.out_wv) p.out_wv[r0 * HD + i] = 0.0f;
-            else if (p.out_f16) static_cast<__half*>(p.out)[r0 * HD + i] = __float2half(0.0f);
-            else static_cast<float*>(p.out)[r0 * HD + i] = 0.0f;
+        for (int k = tid; k < Hq * HD; k += blockDim.x) {
+            if (p.out_wv) p.out_wv[r0 * HD + k] = 0.0f;
+            else if (p.out_f16) static_cast<__half*>(p.out)[r0 * HD + k] = __float2half(0.0f);
+            else static_cast<float*>(p.out)[r0 * HD + k] = 0.0f;
         }
         if (p.out_wv)
-            for (int i = tid; i < Hq; i += blockDim.x) {
-                p.out_l[r0 + i] = 0.0f;
-                p.out_m[r0 + i] = -INFINITY;
+            for (int k = tid; k < Hq; k += blockDim.x) {
+                p.out_l[r0 + k] = 0.0f;
+                p.out_m[r0 + k] = -INFINITY;
             }
     }
-    if (cta >= GR) return;
-    const int64_t u0 = static_cast<int64_t>(cta) * W / GR, u1 = static_cast<int64_t>(cta + 1) * W / GR;
-    int b = 0;
-    {
-        int lo = 0, hi = B - 1;
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (prefix[mid] <= u0) lo = mid;
-            else hi = mid - 1;
-        }
-        b = lo;
-    }
+    if (nseg == 0) return;
 
+    // ---- this warp: kv head(s) and place among the warps sharing them ----------
     const int wsub = WPH > 1 ? warp % WPH : 0;
     const int hbase = WPH > 1 ? warp / WPH : warp;
+    const int h1 = (HPW == 2 && hbase + NCW < Hkv) ? hbase + NCW : -1;  // second head, if any
+    const int nh = h1 >= 0 ? 2 : 1;
+    const int hb = HD * (p.st_f16 ? 2 : 4);      // bytes of one staged row of one head
+    const int tt = p.tail_slot > 0 ? p.tail_slot / (2 * hb) : 1;  // staged rows per tail chunk
     HeadState<NT, HD / 16> st[HPW];
+    TileRegs<KV4, HD> tb[R];
     MetaCache mc;
 
-    for (;;) {
-        const Segment sg = make_segment(p, prefix, b, u0, u1);
-
-        // ---- the staged tail goes to shared memory while the pages stream ----------
-        const int tail_bytes = sg.tail * p.st_row_bytes;
-        const bool tail_smem = sg.tail > 0 && 2 * tail_bytes <= p.tail_cap;
-        const int64_t tail_src = static_cast<int64_t>(sg.b) * P * p.st_row_bytes;
-        if (tail_smem) {
-            const uint8_t* sk = static_cast<const uint8_t*>(p.staging_k) + tail_src;
-            const uint8_t* sv = static_cast<const uint8_t*>(p.staging_v) + tail_src;
-            for (int i = tid * 16; i < tail_bytes; i += blockDim.x * 16) {
-                cp_async16(tailbuf + i, sk + i);
-                cp_async16(tailbuf + tail_bytes + i, sv + i);
+    // ---- issuing walk: runs R - 1 items ahead of the math, across segments -------
+    int sidx = 0;
+    Segment si = make_segment(rec(0), p.P, wsub, WPH, nh, tt);
+    int ji = 0;
+    bool idone = false;
+    mc.base = -(1 << 30);
+    warm_segment<P16>(p, si, hbase, h1, HD, wsub, WPH, lane);
+    // issue the next item of the walk into ring slot iphase; one cp.async
+    // group per item (empty for tiles) keeps the group count in step
+    int iphase = 0;
+    auto issue = [&]() {
+        while (!idone && ji >= si.nitems) {
+            if (++sidx >= nseg) {
+                idone = true;
+            } else {
+                si = make_segment(rec(sidx), p.P, wsub, WPH, nh, tt);
+                ji = 0;
+                mc.base = -(1 << 30);
+                warm_segment<P16>(p, si, hbase, h1, HD, wsub, WPH, lane);
             }
-            cp_async_commit();
         }
+        if (!idone) {
+            if (ji < si.ntile) {
+                const int hh = (si.nh == 2) ? (ji & 1) : 0;
+                const int jt = (si.nh == 2) ? (ji >> 1) : ji;
+                const int h = hh ? h1 : hbase;
+                with_slot<R>(iphase, [&](auto k) {
+                    load_tile<KV4, HD, P16>(tb[decltype(k)::value], mc, p, si, jt, h, wsub, WPH, g, c, lane);
+                });
+            } else {
+                const int q = ji - si.ntile;
+                const int hh = q / si.nchunk, chunk = q - hh * si.nchunk;
+                const int n = min(tt, si.ntt - chunk * tt);
+                issue_tail_chunk(tslots + iphase * p.tail_slot, p, si.b, hh ? h1 : hbase, chunk, n, tt, hb, wsub,
+                                 WPH, lane);
+            }
+            ++ji;
+        }
+        cp_async_commit();
+        iphase = (iphase + 1 == R) ? 0 : iphase + 1;
+    };
+    // the item in ring slot `phase`: one copy of the tile math, whatever the slot
+    auto consume = [&](int phase, const Segment& sc, int j) {
+        if (j < sc.ntile) {
+            TileRegs<KV4, HD> cur;
+            with_slot<R>(phase, [&](auto k) { cur = tb[decltype(k)::value]; });
+            if (HPW == 2 && sc.nh == 2 && (j & 1)) attend_tile<KV4, HD, NT, SPLIT>(st[HPW - 1], cur, p.sm_scale_log2);
+            else attend_tile<KV4, HD, NT, SPLIT>(st[0], cur, p.sm_scale_log2);
+        } else {
+            const int q = j - sc.ntile;
+            const int hh = q / sc.nchunk, chunk = q - hh * sc.nchunk;
+            const int n = min(tt, sc.ntt - chunk * tt);
+            cp_async_wait_group<R - 1>();
+            __syncwarp();
+            const uint8_t* slot = tslots + phase * p.tail_slot;
+            if (HPW == 2 && hh)
+                attend_tail_chunk<KV4, HD, NT, SPLIT>(st[HPW - 1], p, slot, slot + tt * hb, n, sc.b, h1, g, c);
+            else
+                attend_tail_chunk<KV4, HD, NT, SPLIT>(st[0], p, slot, slot + tt * hb, n, sc.b, hbase, g, c);
+            __syncwarp();  // the slot is refilled by a later issue
+        }
+    };
+    for (int k = 0; k < R - 1; ++k) issue();
+    int phase = 0;
+    // cross-CTA merges wait until the end: (segment, ticket value) of the
+    // CTA's first [0] and last [1] segment when they are cut, per head
+    int pend_s[2] = {-1, -1};
+    uint32_t pend_t[2][HPW];
 
+    // ---- consuming walk: every segment of the CTA, in order -----------------------
+    for (int cidx = 0; cidx < nseg; ++cidx) {
+        const Segment sc = make_segment(rec(cidx), p.P, wsub, WPH, nh, tt);
+        const int b = sc.b;
 #pragma unroll
         for (int hh = 0; hh < HPW; ++hh) {
-            const int h = hbase + hh * NCW;
-            if (h < Hkv) load_q<KV4, HD, NT, SPLIT>(st[hh], p, sg.b, h, g, c);
-        }
-
-        // ---- committed pages: this warp's tiles, R - 1 ahead of the math ------------
-        const int ntiles = P16 ? sg.npg : (sg.npg * P + 15) >> 4;
-        const int nloc = wsub < ntiles ? (ntiles - 1 - wsub) / WPH + 1 : 0;
-        const int nitems = nloc * HPW;
-        mc.base = -(1 << 30);
-        TileRegs<KV4, HD> tb[R];
-        auto issue = [&](int j, TileRegs<KV4, HD>& T) {
-            const int h = hbase + (HPW == 2 ? (j & 1) : 0) * NCW;
-            if (h < Hkv) load_tile<KV4, HD, P16>(T, mc, p, sg, HPW == 2 ? (j >> 1) : j, h, wsub, WPH, g, c, lane);
-        };
+            const int h = hh ? h1 : hbase;
+            if (sc.nitems > 0 && h >= 0) {
+                load_q<KV4, HD, NT, SPLIT>(st[hh], p, b, h, g, c);
+            } else {
 #pragma unroll
-        for (int r = 0; r < R - 1; ++r)
-            if (r < nitems) issue(r, tb[r]);
-        for (int j0 = 0; j0 < nitems; j0 += R) {
+                for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-            for (int r = 0; r < R; ++r) {
-                const int j = j0 + r;
-                if (j < nitems) {
-                    if (j + R - 1 < nitems) issue(j + R - 1, tb[(r + R - 1) % R]);
-                    if (HPW == 2) {
-                        if (hbase + (r & 1) * NCW < Hkv) attend_tile<KV4, HD, NT, SPLIT>(st[r & 1], tb[r]);
-                    } else {
-                        attend_tile<KV4, HD, NT, SPLIT>(st[0], tb[r]);
+                    for (int col = 0; col < 2; ++col) {
+                        st[hh].m_used[nt][col] = -INFINITY;
+                        st[hh].m_true[nt][col] = -INFINITY;
+                        st[hh].lpart[nt][col] = 0.0f;
                     }
+#pragma unroll
+                    for (int mt = 0; mt < HD / 16; ++mt)
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) st[hh].acc[mt][nt][i] = 0.0f;
                 }
             }
         }
-
-        // ---- staged tail, split across the warps of a head -------------------------
-        if (sg.tail > 0) {
-            const void* kb;
-            const void* vb;
-            if (tail_smem) {
-                cp_async_wait_all();
-                __syncthreads();
-                kb = tailbuf;
-                vb = tailbuf + tail_bytes;
-            } else {
-                kb = static_cast<const uint8_t*>(p.staging_k) + tail_src;
-                vb = static_cast<const uint8_t*>(p.staging_v) + tail_src;
-            }
-#pragma unroll
-            for (int hh = 0; hh < HPW; ++hh) {
-                const int h = hbase + hh * NCW;
-                if (h < Hkv) attend_tail<KV4, HD, NT, SPLIT>(st[hh], p, kb, vb, sg.b, h, wsub, WPH, sg.tail, g, c);
-            }
+        for (int j = 0; j < sc.nitems; ++j) {
+            issue();  // item k + R - 1 into the slot freed by item k - 1
+            consume(phase, sc, j);
+            phase = (phase + 1 == R) ? 0 : phase + 1;
         }
 
-        // ---- finalize: per (head, column) m / l / o[VE] on this thread ----------
-        const int slot_ws = 2 * cta + (u0 >= sg.ub ? 0 : 1);
+        // ---- finalize the segment: per (head, column) m / l / o[VE] ---------------
+        const int slot_ws = sc.pslot;
 #pragma unroll
         for (int hh = 0; hh < HPW; ++hh) {
-            const int h = hbase + hh * NCW;
-            const bool hv = h < Hkv;
+            const int h = hh ? h1 : hbase;
+            if (h < 0) continue;
+            float o_all[NT][NCOLS][VE], m_all[NT][NCOLS], l_all[NT][NCOLS];
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -543,60 +719,78 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
                     l += __shfl_xor_sync(0xffffffffu, l, 4);
                     l += __shfl_xor_sync(0xffffffffu, l, 8);
                     l += __shfl_xor_sync(0xffffffffu, l, 16);
-                    const int gi = SPLIT ? nt * 4 + c : nt * 8 + 2 * c + col;
                     const float mt = st[hh].m_true[nt][col];
                     const float f = (mt == -INFINITY) ? 0.0f : ex2(st[hh].m_used[nt][col] - mt);
-                    l *= f;
-                    float o[VE];
+                    l_all[nt][col] = l * f;
+                    m_all[nt][col] = mt;
 #pragma unroll
                     for (int mi = 0; mi < HD / 16; ++mi) {
                         if (SPLIT) {
-                            o[2 * mi] = (st[hh].acc[mi][nt][0] + st[hh].acc[mi][nt][1]) * f;
-                            o[2 * mi + 1] = (st[hh].acc[mi][nt][2] + st[hh].acc[mi][nt][3]) * f;
+                            o_all[nt][col][2 * mi] = (st[hh].acc[mi][nt][0] + st[hh].acc[mi][nt][1]) * f;
+                            o_all[nt][col][2 * mi + 1] = (st[hh].acc[mi][nt][2] + st[hh].acc[mi][nt][3]) * f;
                         } else {
-                            o[2 * mi] = st[hh].acc[mi][nt][col] * f;
-                            o[2 * mi + 1] = st[hh].acc[mi][nt][col + 2] * f;
+                            o_all[nt][col][2 * mi] = st[hh].acc[mi][nt][col] * f;
+                            o_all[nt][col][2 * mi + 1] = st[hh].acc[mi][nt][col + 2] * f;
                         }
                     }
-                    float m = mt;
-                    if (WPH > 1) {
-                        // stage this warp's state; the head's first warp merges all WPH of them
-                        float* ms = mscratch + (static_cast<int64_t>(warp) * 4 + c) * (HD + 2);
-                        __syncthreads();  // the previous merge finished reading the scratch
-                        if (hv && gi < p.G) {
+                }
+            if (WPH > 1) {
+                // merge the WPH warps of this head through shared memory (named barrier per head)
+                const int bar = 1 + hbase, nthr = WPH * 32;
+                constexpr int PER = NT * NCOLS * 4 * (HD + 2);  // floats per warp
+                named_barrier_sync(bar, nthr);                   // the previous merge finished reading
+                float* ms = mscratch + static_cast<int64_t>(warp) * PER;
 #pragma unroll
-                            for (int e = 0; e < VE; ++e) ms[VE * g + e] = o[e];
-                            if (g == 0) {
-                                ms[HD] = m;
-                                ms[HD + 1] = l;
-                            }
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int col = 0; col < NCOLS; ++col) {
+                        float* mc0 = ms + ((nt * NCOLS + col) * 4 + c) * (HD + 2);
+#pragma unroll
+                        for (int e = 0; e < VE; ++e) mc0[VE * g + e] = o_all[nt][col][e];
+                        if (g == 0) {
+                            mc0[HD] = m_all[nt][col];
+                            mc0[HD + 1] = l_all[nt][col];
                         }
-                        __syncthreads();
-                        if (wsub == 0 && hv && gi < p.G) {
+                    }
+                named_barrier_sync(bar, nthr);
+                if (wsub == 0) {
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                        for (int col = 0; col < NCOLS; ++col) {
+                            const int off = ((nt * NCOLS + col) * 4 + c) * (HD + 2);
                             float M = -INFINITY;
                             for (int ww = 0; ww < WPH; ++ww)
-                                M = fmaxf(M, mscratch[(static_cast<int64_t>(warp + ww) * 4 + c) * (HD + 2) + HD]);
+                                M = fmaxf(M, mscratch[static_cast<int64_t>(warp + ww) * PER + off + HD]);
                             float L = 0.0f;
                             float oo[VE];
 #pragma unroll
                             for (int e = 0; e < VE; ++e) oo[e] = 0.0f;
                             for (int ww = 0; ww < WPH; ++ww) {
-                                const float* mw = mscratch + (static_cast<int64_t>(warp + ww) * 4 + c) * (HD + 2);
+                                const float* mw = mscratch + static_cast<int64_t>(warp + ww) * PER + off;
                                 const float fw = (mw[HD] == -INFINITY) ? 0.0f : ex2(mw[HD] - M);
                                 L += mw[HD + 1] * fw;
 #pragma unroll
                                 for (int e = 0; e < VE; ++e) oo[e] += mw[VE * g + e] * fw;
                             }
-                            m = M;
-                            l = L;
+                            m_all[nt][col] = M;
+                            l_all[nt][col] = L;
 #pragma unroll
-                            for (int e = 0; e < VE; ++e) o[e] = oo[e];
+                            for (int e = 0; e < VE; ++e) o_all[nt][col][e] = oo[e];
                         }
-                    }
-                    if (!hv || gi >= p.G || wsub != 0) continue;
-                    const int hq = h * p.G + gi;
-                    const int64_t orow = static_cast<int64_t>(sg.b) * Hq + hq;
-                    if (sg.complete) {
+                }
+            }
+            if (wsub != 0) continue;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int col = 0; col < NCOLS; ++col) {
+                    const int gi = SPLIT ? nt * 4 + c : nt * 8 + 2 * c + col;
+                    if (gi >= p.G) continue;
+                    const int64_t orow = static_cast<int64_t>(b) * Hq + h * p.G + gi;
+                    const float* o = o_all[nt][col];
+                    const float m = m_all[nt][col], l = l_all[nt][col];
+                    if (sc.complete) {
                         const int64_t base_o = orow * HD + VE * g;
                         if (p.out_wv) {
 #pragma unroll
@@ -621,7 +815,7 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
                             }
                         }
                     } else {
-                        const int64_t prow = static_cast<int64_t>(slot_ws) * Hq + hq;
+                        const int64_t prow = static_cast<int64_t>(slot_ws) * Hq + (orow - static_cast<int64_t>(b) * Hq);
                         float* wp = p.ws_acc + prow * HD + VE * g;
 #pragma unroll
                         for (int e = 0; e < VE; e += 4)
@@ -632,100 +826,48 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
                         }
                     }
                 }
-        }
-
-        if (!sg.complete) {
-            // ---- last covering CTA merges the partials of sequence b (one pass) ------
-            __threadfence();
-            __syncthreads();
-            const int c_first = cta_of_unit(sg.ub, W, GR);
-            const int c_last = cta_of_unit(sg.ue - 1, W, GR);
-            if (tid == 0) {
-                const uint32_t prev = atomicAdd(&p.tickets[sg.b], 1u);
-                sm_last = (prev == static_cast<uint32_t>(c_last - c_first)) ? 1 : 0;
-            }
-            __syncthreads();
-            if (sm_last) {
-                __threadfence();
-                const int ncov = c_last - c_first + 1;
-                for (int it = tid; it < Hq * (HD / 4); it += blockDim.x) {
-                    const int hq = it / (HD / 4), d4 = (it - hq * (HD / 4)) * 4;
-                    float M = -INFINITY, L = 0.0f;
-                    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-                    for (int k0 = 0; k0 < ncov; k0 += 4) {
-                        float mj[4], lj[4];
-                        float4 vj[4];
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            mj[u] = -INFINITY;
-                            lj[u] = 0.0f;
-                            vj[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-                            if (k0 + u < ncov) {
-                                const int cc = c_first + k0 + u;
-                                const int sl = 2 * cc + ((static_cast<int64_t>(cc) * W / GR) >= sg.ub ? 0 : 1);
-                                const int64_t prow = static_cast<int64_t>(sl) * Hq + hq;
-                                mj[u] = __ldcg(p.ws_m + prow);
-                                lj[u] = __ldcg(p.ws_l + prow);
-                                vj[u] = __ldcg(reinterpret_cast<const float4*>(p.ws_acc + prow * HD + d4));
-                            }
-                        }
-                        float Mn = M;
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) Mn = fmaxf(Mn, mj[u]);
-                        const float fo = (M == -INFINITY) ? 0.0f : ex2(M - Mn);
-                        L *= fo;
-                        a.x *= fo;
-                        a.y *= fo;
-                        a.z *= fo;
-                        a.w *= fo;
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            const float fj = (mj[u] == -INFINITY) ? 0.0f : ex2(mj[u] - Mn);
-                            L += lj[u] * fj;
-                            a.x += vj[u].x * fj;
-                            a.y += vj[u].y * fj;
-                            a.z += vj[u].z * fj;
-                            a.w += vj[u].w * fj;
-                        }
-                        M = Mn;
-                    }
-                    const int64_t orow = static_cast<int64_t>(sg.b) * Hq + hq;
-                    const int64_t base_o = orow * HD + d4;
-                    if (p.out_wv) {
-                        *reinterpret_cast<float4*>(p.out_wv + base_o) = a;
-                        if (d4 == 0) {
-                            p.out_l[orow] = L;
-                            p.out_m[orow] = M * kLn2;
-                        }
-                    } else {
-                        const float inv = 1.0f / L;
-                        if (p.out_f16) {
-                            __half2* op = reinterpret_cast<__half2*>(static_cast<__half*>(p.out) + base_o);
-                            op[0] = __floats2half2_rn(a.x * inv, a.y * inv);
-                            op[1] = __floats2half2_rn(a.z * inv, a.w * inv);
-                        } else {
-                            *reinterpret_cast<float4*>(static_cast<float*>(p.out) + base_o) =
-                                make_float4(a.x * inv, a.y * inv, a.z * inv, a.w * inv);
-                        }
-                    }
-                }
-                if (tid == 0) p.tickets[sg.b] = 0u;  // leave the workspace reusable
+            if (sc.complete) continue;
+            // publish the partial: the ticket's release orders the warp's stores
+            // (__syncwarp), its value is read after the last segment
+            __syncwarp();
+            uint32_t prev = 0;
+            if (lane == 0) prev = ticket_add(&p.tickets[static_cast<int64_t>(b) * Hkv + h]);
+            if (cidx == 0) {
+                pend_s[0] = cidx;
+                pend_t[0][hh] = prev;
+            } else {
+                pend_s[1] = cidx;
+                pend_t[1][hh] = prev;
             }
         }
-        __syncthreads();  // tail buffer and merge scratch are free for the next segment
-
-        // ---- next non-empty sequence inside [u0, u1) ------------------------------
-        if (sg.ue >= u1) break;
-        ++b;
-        while (b < B && prefix[b + 1] == prefix[b]) ++b;
-        if (b >= B) break;
     }
+
+    // ---- merges of the cut sequences whose last covering CTA this is ---------------
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        if (wsub != 0 || pend_s[k] < 0) continue;
+        const int4 r0 = rec(pend_s[k])[0], r1 = rec(pend_s[k])[1];
+        const int b = r0.x, pbase = r1.y, ncov = r1.z;
+        const uint32_t need = static_cast<uint32_t>(ncov - 1);
+#pragma unroll
+        for (int hh = 0; hh < HPW; ++hh) {
+            const int h = hh ? h1 : hbase;
+            if (h < 0) continue;
+            const uint32_t prev = __shfl_sync(0xffffffffu, pend_t[k][hh], 0);
+            if (prev != need) continue;
+            __threadfence();
+            merge_partials<HD>(p, b, h, pbase, ncov, lane);
+        }
+    }
+    cp_async_wait_all();  // no copy outlives the CTA
 }
 
 template <bool KV4, int HD, int NT, bool SPLIT, bool P16, int HPW, int R, int NW>
 mg_status launch_one(const DecodeParams& p, const DecodePlan& pl, cudaStream_t s) {
     auto k = paged_decode_kernel<KV4, HD, NT, SPLIT, P16, HPW, R, NW>;
-    if (pl.nconsumers > NW) return set_error(MG_ERR_UNSUPPORTED, "decode plan wants %d warps > %d", pl.nconsumers, NW);
+    if (pl.nconsumers > NW || pl.ring != R)
+        return set_error(MG_ERR_UNSUPPORTED, "decode plan (%d warps, ring %d) does not match the kernel (%d, %d)",
+                         pl.nconsumers, pl.ring, NW, R);
     static int64_t attr_set[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -750,20 +892,22 @@ mg_status launch_one(const DecodeParams& p, const DecodePlan& pl, cudaStream_t s
     return check_launch("paged_decode_kernel");
 }
 
-// Kernel shapes (the planner's choice, DecodePlan::nwarps / hpw):
-//   head_dim 64, one n-tile:   16 warps, one kv head per warp (two tiles in
-//                              flight for INT8, three for INT4) or two heads
-//                              per warp (num_kv_heads 17..32);
-//   otherwise, <= 8 kv heads:  8 warps with up to 255 registers, two tiles in flight;
-//   otherwise, 9..16 kv heads: 16 warps, one tile at a time.
+// Kernel shapes (the planner's choice, DecodePlan::nwarps / hpw); the tile
+// ring depth of each is decode_ring().
 template <bool KV4, int HD, int NT, bool SPLIT, bool P16>
 mg_status launch_h(const DecodeParams& p, const DecodePlan& pl, cudaStream_t s) {
     if constexpr (HD == 64 && NT == 1) {
-        if (pl.hpw == 2) return launch_one<KV4, HD, NT, SPLIT, P16, 2, 2, kWarps>(p, pl, s);
-        return launch_one<KV4, HD, NT, SPLIT, P16, 1, (KV4 ? 3 : 2), kWarps>(p, pl, s);
+        if (pl.hpw == 2)
+            return launch_one<KV4, HD, NT, SPLIT, P16, 2, decode_ring(KV4, HD, NT, 2, kWarps), kWarps>(p, pl, s);
+        if (pl.nwarps == kWarpsDeep)
+            return launch_one<KV4, HD, NT, SPLIT, P16, 1, decode_ring(KV4, HD, NT, 1, kWarpsDeep), kWarpsDeep>(p, pl,
+                                                                                                              s);
+        return launch_one<KV4, HD, NT, SPLIT, P16, 1, decode_ring(KV4, HD, NT, 1, kWarps), kWarps>(p, pl, s);
     } else {
-        if (pl.nwarps == kWarpsWide) return launch_one<KV4, HD, NT, SPLIT, P16, 1, 2, kWarpsWide>(p, pl, s);
-        return launch_one<KV4, HD, NT, SPLIT, P16, 1, 1, kWarps>(p, pl, s);
+        if (pl.nwarps == kWarpsWide)
+            return launch_one<KV4, HD, NT, SPLIT, P16, 1, decode_ring(KV4, HD, NT, 1, kWarpsWide), kWarpsWide>(p, pl,
+                                                                                                              s);
+        return launch_one<KV4, HD, NT, SPLIT, P16, 1, decode_ring(KV4, HD, NT, 1, kWarps), kWarps>(p, pl, s);
     }
 }
 

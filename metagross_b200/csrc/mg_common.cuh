@@ -233,6 +233,17 @@ __device__ __forceinline__ void cp_async16(void* dst_smem, const void* src_gmem)
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+// Wait until at most N of this thread's most recent cp.async groups are pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+// Non-blocking hint: bring the line holding ptr into L1.
+__device__ __forceinline__ void prefetch_l1(const void* ptr) { asm volatile("prefetch.global.L1 [%0];" ::"l"(ptr)); }
+// Barrier among the nthreads (a multiple of 32) threads that use barrier id.
+__device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
 
 // Programmatic dependent launch: block until the grids this one depends on
 // have completed (a no-op when launched without the attribute), and let the

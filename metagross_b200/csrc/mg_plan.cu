@@ -1,0 +1,301 @@
+// Per-step decode plan: how the batch's work is split over the CTAs of the
+// paged decode-attention kernel.  It depends only on the sequence lengths
+// (and the page size), which every layer of a decode step shares, so one
+// plan serves all the step's attention launches.
+//
+// Work is counted in "units": one committed page, or the staged tail (< P
+// rows), of one sequence.  Two partitions:
+//   chunk     when the non-empty sequences fit on the SMs: each sequence gets
+//             k_b = ceil(U_b / S) near-equal chunks with S the smallest chunk
+//             size for which sum_b k_b <= #CTAs (so the longest chunk is as
+//             short as possible), and every CTA runs exactly one chunk of one
+//             sequence -- no CTA pays for a second sequence;
+//   stream-K  otherwise: CTA c takes units [c*W/G, (c+1)*W/G) of the
+//             flattened list, i.e. a few whole short sequences plus the cut
+//             ends of at most two others.
+// A sequence cut into several pieces gets one partial (m, l, acc) slot per
+// piece, contiguous from pbase; the last piece to finish merges them.
+#include "mg_attention.cuh"
+
+namespace mg {
+
+namespace {
+
+constexpr int kPlanThreads = 1024;
+
+struct PlanParams {
+    const int32_t* seq_lens;
+    int32_t uniform_len;  // >= 0: every sequence has this many committed tokens
+    int batch, P, max_blocks, has_staging;
+    int grid;
+    PlanLayout lay;
+    int32_t* plan;
+    int32_t* status;
+};
+
+__device__ __forceinline__ int block_sum(int v, int* scratch) {
+    int tot;
+    block_exclusive_scan(v, scratch, &tot);
+    return tot;
+}
+
+__device__ __forceinline__ int block_max_int(int v, int* scratch) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __syncthreads();
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    int r = lane < static_cast<int>(blockDim.x >> 5) ? scratch[lane] : 0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) r = max(r, __shfl_xor_sync(0xffffffffu, r, o));
+    return r;
+}
+
+// Exclusive scan of vals[0..n) into out[0..n] (out[n] = total), block-wide.
+__device__ __forceinline__ int block_scan_array(const int* vals, int* out, int n, int* scratch) {
+    int base = 0;
+    for (int start = 0; start < n; start += blockDim.x) {
+        const int i = start + threadIdx.x;
+        const int v = i < n ? vals[i] : 0;
+        int tot;
+        const int ex = block_exclusive_scan(v, scratch, &tot);
+        if (i < n) out[i] = base + ex;
+        base += tot;
+    }
+    if (threadIdx.x == 0) out[n] = base;
+    __syncthreads();
+    return base;
+}
+
+// Record k of CTA cta, whose records start at flat index off: into the flat
+// array, and into the CTA's inline area when k < kPlanInline.
+__device__ __forceinline__ void write_rec(const PlanParams& pp, int cta, int off, int k, int b, int lo, int npg,
+                                          int tail, int pslot, int pbase, int ncov) {
+    const int4 r0 = make_int4(b, lo, npg, tail), r1 = make_int4(pslot, pbase, ncov, 0);
+    int4* f = reinterpret_cast<int4*>(pp.plan + pp.lay.off_flat + static_cast<int64_t>(off + k) * 8);
+    f[0] = r0;
+    f[1] = r1;
+    if (k < kPlanInline) {
+        int4* r = reinterpret_cast<int4*>(pp.plan + pp.lay.off_recs + (static_cast<int64_t>(cta) * kPlanInline + k) * 8);
+        r[0] = r0;
+        r[1] = r1;
+    }
+}
+
+__global__ void __launch_bounds__(kPlanThreads, 1) decode_plan_kernel(const PlanParams pp) {
+    extern __shared__ __align__(16) int psm[];
+    __shared__ int scratch[33];
+    grid_dependency_wait();
+    grid_launch_dependents();
+    const int B = pp.batch, P = pp.P, G = pp.grid;
+    int* len = psm;             // [B]
+    int* units = len + B;       // [B]
+    int* pre = units + B;       // [B + 1] unit prefix
+    int* aux = pre + B + 1;     // [B + 1] chunks per sequence / pieces per sequence, then their prefix
+    int* aux2 = aux + B + 1;    // [B + 1] partial-slot prefix
+    int* tmp = aux2 + B + 1;    // [max(B, 2 * grid + 1)]
+
+    // ---- lengths and units --------------------------------------------------------
+    int nonempty = 0, maxu = 0;
+    for (int b = threadIdx.x; b < B; b += blockDim.x) {
+        int l;
+        if (pp.uniform_len >= 0) {
+            l = pp.uniform_len;
+        } else {
+            l = pp.seq_lens[b];
+            if (l < 0 || l / P > pp.max_blocks) {
+                flag(pp.status, MG_DEV_BAD_ARGUMENT);
+                l = 0;
+            }
+        }
+        const int np = l / P;
+        const int u = np + ((pp.has_staging && l - np * P > 0) ? 1 : 0);
+        len[b] = l;
+        units[b] = u;
+        nonempty += u > 0;
+        maxu = max(maxu, u);
+    }
+    __syncthreads();
+    nonempty = block_sum(nonempty, scratch);
+    maxu = block_max_int(maxu, scratch);
+    const int W = block_scan_array(units, pre, B, scratch);
+
+    // ---- empty sequences (written as zeros by the attention CTAs) ------------------
+    for (int b = threadIdx.x; b < B; b += blockDim.x) tmp[b] = units[b] == 0 ? 1 : 0;
+    __syncthreads();
+    const int n_empty = block_scan_array(tmp, aux2, B, scratch);
+    for (int b = threadIdx.x; b < B; b += blockDim.x)
+        if (units[b] == 0) pp.plan[pp.lay.off_empty + aux2[b]] = b;
+
+    const bool chunk = W > 0 && nonempty <= G;
+    int used = 0;
+    if (chunk) {
+        // ---- smallest chunk size S with sum_b ceil(U_b / S) <= G -----------------
+        int lo = (W + G - 1) / G, hi = maxu > lo ? maxu : lo;
+        while (lo < hi) {
+            const int mid = lo + (hi - lo) / 2;
+            int need = 0;
+            for (int b = threadIdx.x; b < B; b += blockDim.x) need += (units[b] + mid - 1) / mid;
+            need = block_sum(need, scratch);
+            if (need <= G) hi = mid;
+            else lo = mid + 1;
+        }
+        const int S = lo;
+        for (int b = threadIdx.x; b < B; b += blockDim.x) tmp[b] = (units[b] + S - 1) / S;
+        __syncthreads();
+        used = block_scan_array(tmp, aux, B, scratch);  // aux[b]: first CTA of sequence b
+        for (int b = threadIdx.x; b < B; b += blockDim.x) tmp[b] = tmp[b] > 1 ? tmp[b] : 0;
+        __syncthreads();
+        block_scan_array(tmp, aux2, B, scratch);  // aux2[b]: first partial slot of sequence b
+        for (int b = threadIdx.x; b < B; b += blockDim.x) {
+            const int u = units[b];
+            const int k = aux[b + 1] - aux[b];
+            const int np = len[b] / P;
+            const int tb = pp.has_staging ? len[b] - np * P : 0;
+            for (int j = 0; j < k; ++j) {
+                const int ulo = static_cast<int>(static_cast<int64_t>(j) * u / k);
+                const int uhi = static_cast<int>(static_cast<int64_t>(j + 1) * u / k);
+                const int npg = max(0, min(uhi, np) - ulo);
+                const int tail = (uhi == u && tb > 0) ? tb : 0;
+                const int cta = aux[b] + j;
+                write_rec(pp, cta, cta, 0, b, ulo, npg, tail, k > 1 ? aux2[b] + j : -1, aux2[b], k);
+                pp.plan[pp.lay.off_counts + cta] = 1;
+                pp.plan[pp.lay.off_offs + cta] = cta;
+            }
+        }
+    } else if (W > 0) {
+        // ---- stream-K: even unit ranges ------------------------------------------
+        const int GR = W < G ? W : G;
+        used = GR;
+        auto cta_of_unit = [&](int64_t u) {
+            int l = 0, h = GR - 1;
+            while (l < h) {
+                const int mid = (l + h + 1) >> 1;
+                if ((static_cast<int64_t>(mid) * W) / GR <= u) l = mid;
+                else h = mid - 1;
+            }
+            return l;
+        };
+        for (int b = threadIdx.x; b < B; b += blockDim.x) {
+            int pieces = 0;
+            if (units[b] > 0) pieces = cta_of_unit(pre[b + 1] - 1) - cta_of_unit(pre[b]) + 1;
+            aux[b] = pieces;
+            tmp[b] = pieces > 1 ? pieces : 0;
+        }
+        __syncthreads();
+        block_scan_array(tmp, aux2, B, scratch);  // aux2[b]: first partial slot of sequence b
+        // segments per CTA, their prefix (flat offsets), then the records
+        auto first_seq = [&](int64_t u0) {
+            int l = 0, h = B - 1;
+            while (l < h) {
+                const int mid = (l + h + 1) >> 1;
+                if (pre[mid] <= u0) l = mid;
+                else h = mid - 1;
+            }
+            return l;
+        };
+        for (int c = threadIdx.x; c < G; c += blockDim.x) {
+            int k = 0;
+            if (c < GR) {
+                const int64_t u0 = static_cast<int64_t>(c) * W / GR, u1 = static_cast<int64_t>(c + 1) * W / GR;
+                for (int b = first_seq(u0); b < B && pre[b] < u1; ++b) k += pre[b + 1] > pre[b];
+            }
+            tmp[c] = k;
+        }
+        __syncthreads();
+        block_scan_array(tmp, tmp + G, G, scratch);  // tmp[G..2G]: flat offsets
+        const int* offs = tmp + G;
+        for (int c = threadIdx.x; c < GR; c += blockDim.x) {
+            const int64_t u0 = static_cast<int64_t>(c) * W / GR, u1 = static_cast<int64_t>(c + 1) * W / GR;
+            int k = 0;
+            for (int b = first_seq(u0); b < B && pre[b] < u1; ++b) {
+                const int ub = pre[b], ue = pre[b + 1];
+                if (ue == ub) continue;
+                const int lo = static_cast<int>((u0 > ub ? u0 : ub) - ub);
+                const int hi = static_cast<int>((u1 < ue ? u1 : ue) - ub);
+                const int np = len[b] / P;
+                const int tb = pp.has_staging ? len[b] - np * P : 0;
+                const int npg = max(0, min(hi, np) - lo);
+                const int tail = (hi == ue - ub && tb > 0) ? tb : 0;
+                const bool whole = lo == 0 && hi == ue - ub;
+                const int first = cta_of_unit(ub);
+                write_rec(pp, c, offs[c], k, b, lo, npg, tail, whole ? -1 : aux2[b] + (c - first), aux2[b], aux[b]);
+                ++k;
+            }
+            pp.plan[pp.lay.off_counts + c] = k;
+            pp.plan[pp.lay.off_offs + c] = offs[c];
+        }
+    }
+    for (int c = used + threadIdx.x; c < G; c += blockDim.x) pp.plan[pp.lay.off_counts + c] = 0;
+    if (threadIdx.x == 0) {
+        int32_t* h = pp.plan;
+        h[0] = kPlanMagic;
+        h[1] = B;
+        h[2] = G;
+        h[3] = 0;
+        h[4] = n_empty;
+        h[5] = chunk ? 1 : 2;
+        h[6] = W;
+        h[7] = used;
+        h[8] = pp.has_staging;
+    }
+}
+
+}  // namespace
+
+PlanLayout plan_layout(int batch, int grid) {
+    PlanLayout L{};
+    L.off_counts = 16;
+    L.off_offs = L.off_counts + grid;
+    L.off_recs = ((L.off_offs + grid) + 7) / 8 * 8;
+    L.off_flat = L.off_recs + grid * kPlanInline * 8;
+    L.off_empty = L.off_flat + (batch + grid) * 8;
+    L.words = L.off_empty + batch;
+    return L;
+}
+
+mg_status launch_decode_plan(const int32_t* seq_lens, int32_t uniform_len, int batch, int P, int max_blocks,
+                             int has_staging, int32_t* plan, int64_t plan_bytes, int32_t* status, cudaStream_t s) {
+    const int G = sm_count();
+    const PlanLayout lay = plan_layout(batch, G);
+    MG_REQUIRE(plan && plan_bytes >= static_cast<int64_t>(lay.words) * 4, "decode plan buffer too small: %lld < %lld",
+               (long long)plan_bytes, (long long)lay.words * 4);
+    MG_REQUIRE((reinterpret_cast<uintptr_t>(plan) & 15u) == 0, "decode plan buffer must be 16-byte aligned");
+    PlanParams pp{};
+    pp.seq_lens = seq_lens;
+    pp.uniform_len = uniform_len;
+    pp.batch = batch;
+    pp.P = P;
+    pp.max_blocks = max_blocks;
+    pp.has_staging = has_staging;
+    pp.grid = G;
+    pp.lay = lay;
+    pp.plan = plan;
+    pp.status = status;
+    const size_t smem = (static_cast<size_t>(6) * batch + 3 + 2 * G + 1) * sizeof(int);
+    static int64_t attr_set[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (smem > 48 * 1024 && (dev < 0 || dev >= 64 || attr_set[dev] < static_cast<int64_t>(smem))) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(decode_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return set_error(MG_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+        if (dev >= 0 && dev < 64) attr_set[dev] = static_cast<int64_t>(smem);
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(kPlanThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_plan_kernel, pp);
+    if (e != cudaSuccess) return set_error(MG_ERR_CUDA, "decode_plan_kernel launch: %s", cudaGetErrorString(e));
+    return check_launch("decode_plan_kernel");
+}
+
+}  // namespace mg

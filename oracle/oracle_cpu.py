@@ -67,6 +67,8 @@ def time_decode_sample(w, seconds=10.0, seed=0, max_seqs=8):
     P, hkv, d, hq, kv = w["page"], w["hkv"], w["d"], w["hq"], w["kv"]
     if w["ctx"] == "uniform128_2048":
         ctx = rng.integers(128, 2049, size=max_seqs)
+    elif w["ctx"] == "lognormal2048":
+        ctx = np.exp(rng.normal(np.log(2048.0), 1.0, size=max_seqs)).round().clip(2, 32768).astype(np.int64) - 1
     else:
         ctx = np.full(max_seqs, int(w["ctx"]) - 1)
     nseq = max_seqs
