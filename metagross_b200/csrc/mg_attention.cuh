@@ -54,6 +54,7 @@ constexpr int kWarpsDeep = 12;  // head_dim 64, one n-tile: <= 168 registers, a 
 constexpr int kWarpsWide = 8;   // head_dim 128 or two n-tiles with <= 8 kv heads: <= 255 registers
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 2^8 in fp16
 constexpr int kMetaLanes = 32;             // page ids cached per warp (one per lane)
+constexpr int kPrefetchTiles = 8;          // L2 prefetch distance of a warp's tile stream (tiles)
 
 // Work items (tiles or staged-tail chunks) in flight per warp, by register
 // budget (R - 1 of them are loading while one is computed):

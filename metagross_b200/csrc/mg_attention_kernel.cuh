@@ -352,11 +352,12 @@ __device__ __forceinline__ void warm_segment(const DecodeParams& p, const Segmen
 }
 
 // Issue the global loads of the warp's local tile jt (segment tile
-// wsub + jt * wph) of kv head h into T.  Warp-uniform.
+// wsub + jt * wph; the warp has nloc in the segment) of kv head h into T.
+// Warp-uniform.
 template <bool KV4, int HD, bool P16>
 __device__ __forceinline__ void load_tile(TileRegs<KV4, HD>& T, MetaCache& mc, const DecodeParams& p,
-                                          const Segment& sg, int jt, int h, int wsub, int wph, int g, int c,
-                                          int lane) {
+                                          const Segment& sg, int jt, int nloc, int h, int wsub, int wph, int g,
+                                          int c, int lane) {
     using C = Cfg<KV4, HD, 1>;
     const int rs = p.Hkv * C::ROWB;  // bytes per token row of a page
     if (P16) {
@@ -376,6 +377,14 @@ __device__ __forceinline__ void load_tile(TileRegs<KV4, HD>& T, MetaCache& mc, c
         for (int r = 0; r < 4; ++r) {
             const int row = 2 * c + (r & 1) + (r >> 1) * 8;
             ldg_words<C::VCHB>(vb + row * rs + g * C::VCHB, T.v[r]);
+        }
+        // L2 prefetch of the warp's tile kPrefetchTiles ahead: lane l brings K row l
+        // (l < 16) or V row l - 16 of this head, so the register ring reads from L2
+        const int ja = jt + kPrefetchTiles;
+        if (ja < nloc && ja < mc.base + kMetaLanes) {
+            const int32_t pa = __shfl_sync(0xffffffffu, mc.pid, ja - mc.base);
+            const uint8_t* pool = lane < 16 ? p.k_pool : p.v_pool;
+            prefetch_l2(pool + static_cast<int64_t>(pa) * p.page_bytes + (lane & 15) * rs + h * C::ROWB);
         }
     } else {
         const int P = p.P;
@@ -630,8 +639,9 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
                 const int hh = (si.nh == 2) ? (ji & 1) : 0;
                 const int jt = (si.nh == 2) ? (ji >> 1) : ji;
                 const int h = hh ? h1 : hbase;
+                const int nloc = si.nh == 2 ? (si.ntile >> 1) : si.ntile;
                 with_slot<R>(iphase, [&](auto k) {
-                    load_tile<KV4, HD, P16>(tb[decltype(k)::value], mc, p, si, jt, h, wsub, WPH, g, c, lane);
+                    load_tile<KV4, HD, P16>(tb[decltype(k)::value], mc, p, si, jt, nloc, h, wsub, WPH, g, c, lane);
                 });
             } else {
                 const int q = ji - si.ntile;

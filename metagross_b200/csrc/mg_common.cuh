@@ -240,6 +240,8 @@ __device__ __forceinline__ void cp_async_wait_group() {
 }
 // Non-blocking hint: bring the line holding ptr into L1.
 __device__ __forceinline__ void prefetch_l1(const void* ptr) { asm volatile("prefetch.global.L1 [%0];" ::"l"(ptr)); }
+// Non-blocking hint: bring the line holding ptr into L2 (coherent with every writer).
+__device__ __forceinline__ void prefetch_l2(const void* ptr) { asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr)); }
 // Barrier among the nthreads (a multiple of 32) threads that use barrier id.
 __device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
