@@ -229,13 +229,16 @@ MG_API int64_t mg_paged_decode_plan_bytes(int32_t batch);
 MG_API mg_status mg_paged_decode_plan(const mg_cache_layout* layout, const int32_t* seq_lens, int32_t batch,
                                int32_t with_staging, void* plan, int64_t plan_bytes, int32_t* dev_status,
                                mg_stream_t stream);
-/* mg_paged_decode_attention for callers that cannot allocate device memory:
- * no workspace argument; the workspace lives in a 4 MiB static device array
- * inside libmgb200.so (found on the first call on each device, which should
- * come before any stream capture begins).  Calls whose workspace
+/* mg_paged_decode_attention for callers that cannot call cudaMalloc (a
+ * serving runtime whose pool allocator owns all device memory, or a decode
+ * loop that must not pay cudaMalloc's device synchronisation): no workspace
+ * argument; the workspace lives in a 4 MiB static device array inside
+ * libmgb200.so, held by every GPU that loads the library until exit.  The
+ * first call on each device looks its address up (make that call before any
+ * stream capture begins).  Calls whose workspace
  * (mg_paged_decode_workspace_bytes) exceeds 4 MiB are rejected with
  * MG_ERR_INVALID_ARGUMENT.  Each call zeroes the merge counters on `stream`
- * first.  Calls that overlap on one device share the array and race.  No
+ * first.  Calls that overlap on the GPU share the array and race.  No
  * counterpart in the reference. */
 MG_API mg_status mg_paged_decode_attention_noalloc(const mg_cache_layout* layout, const mg_layer_ptrs* layer,
                                             const int32_t* block_tables, const int32_t* seq_lens,

@@ -1,14 +1,21 @@
 // mg_paged_decode_attention_noalloc: the batched decode attention with its
 // workspace (merge counters, partial slots, decode plan) in a fixed static
-// device array instead of caller memory, for callers that cannot allocate.
+// device array instead of caller memory.  It is for callers that cannot call
+// cudaMalloc: serving runtimes whose own pool allocator has reserved all
+// device memory up front (a raw cudaMalloc there fails or fragments the
+// pool), and latency-critical decode loops where cudaMalloc / cudaFree would
+// synchronize the device and stall the other streams.
 //
-// The scratch is one file-scope __device__ array of kNoAllocScratchBytes,
-// found per device with cudaGetSymbolAddress on the first call there (make
-// that first call before any stream capture begins).  Every call zeroes the
-// merge counters at its start (a memset on the call's stream; the kernels
-// leave them zero too) and then runs mg_paged_decode_attention on the array.
-// Calls that overlap on the device share the array and race: run one at a
-// time per device.
+// The scratch is one file-scope __device__ array of kNoAllocScratchBytes;
+// every GPU that loads the library holds it until the process exits.  In
+// host code its name is only a host-side stand-in, so the device address is
+// looked up with cudaGetSymbolAddress, once per device with that device
+// current, on the first call there (make that first call before any stream
+// capture begins), and that address is what the kernels get.  Every call
+// zeroes the merge counters at its start (a memset on the call's stream; the
+// array keeps whatever the previous call left) and then runs
+// mg_paged_decode_attention on the array.  Calls that overlap on the GPU
+// share the array and race: run one at a time per device.
 #include <mutex>
 
 #include "mg_common.cuh"
