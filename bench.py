@@ -341,8 +341,15 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="gpt2_int8")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="override the workload's layer count (a small case for profiling; the default run uses "
+                         "the workload's own depth)")
     args = ap.parse_args()
-    w = WORKLOADS[args.workload]
+    w = dict(WORKLOADS[args.workload])
+    if args.layers is not None:
+        if args.layers < 1:
+            raise SystemExit("--layers must be >= 1")
+        w["layers"] = args.layers
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -223,12 +223,14 @@ MG_API int64_t mg_paged_decode_workspace_bytes(const mg_cache_layout* layout, in
  * paged_attention op handles one sequence per call, csrc/bindings.cpp:82-106).
  * plan: mg_paged_decode_plan_bytes(batch) bytes, 16-byte aligned, device
  * memory; with_staging says whether the attention calls will fold the staged
- * tails in (it must match their staging pointers).  Invalid lengths set
- * MG_DEV_BAD_ARGUMENT and are planned as empty. */
+ * tails in (it must match their staging pointers).  The plan also keeps a
+ * copy of each CTA's first block-table entries, so it is rebuilt whenever the
+ * block tables or seq_lens change.  Invalid lengths set MG_DEV_BAD_ARGUMENT
+ * and are planned as empty. */
 MG_API int64_t mg_paged_decode_plan_bytes(int32_t batch);
-MG_API mg_status mg_paged_decode_plan(const mg_cache_layout* layout, const int32_t* seq_lens, int32_t batch,
-                               int32_t with_staging, void* plan, int64_t plan_bytes, int32_t* dev_status,
-                               mg_stream_t stream);
+MG_API mg_status mg_paged_decode_plan(const mg_cache_layout* layout, const int32_t* block_tables,
+                               const int32_t* seq_lens, int32_t batch, int32_t with_staging, void* plan,
+                               int64_t plan_bytes, int32_t* dev_status, mg_stream_t stream);
 /* mg_paged_decode_attention for callers that cannot call cudaMalloc (a
  * serving runtime whose pool allocator owns all device memory, or a decode
  * loop that must not pay cudaMalloc's device synchronisation): no workspace

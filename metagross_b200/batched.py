@@ -22,10 +22,11 @@ A decode/prefill step is:
   for layer: cache.append(layer, k, v) # quantize filled pages, stage the rest
              out = cache.attend(layer, q)
 
-The first ``attend`` after the lengths change (begin_step, truncate, free,
-reset) builds the step's decode plan -- the split of the batch's pages over
-the SMs -- and the other layers reuse it.  Code that writes ``seq_lens``
-directly must call ``invalidate_plan()``.
+The first ``attend`` after the lengths or block tables change (begin_step,
+truncate, free, reset) builds the step's decode plan -- the split of the
+batch's pages over the SMs, with a copy of each CTA's first page ids -- and
+the other layers reuse it.  Code that writes ``seq_lens`` or
+``block_tables`` directly must call ``invalidate_plan()``.
 """
 from __future__ import annotations
 
@@ -124,7 +125,7 @@ class BatchedPagedKVCache:
                            self.n_new, k_new, v_new, self.status)
 
     def invalidate_plan(self) -> None:
-        """Mark the decode plan stale (after writing seq_lens directly)."""
+        """Mark the decode plan stale (after writing seq_lens or block_tables directly)."""
         self._plan_ok = False
 
     def _decode_plan(self) -> torch.Tensor:

@@ -462,7 +462,8 @@ void decode_plan(torch::Tensor k_pool, torch::Tensor block_tables, torch::Tensor
     L.head_dim = static_cast<int32_t>(i4 ? k_pool.size(3) * 2 : k_pool.size(3));
     L.max_blocks = static_cast<int32_t>(block_tables.size(1));
     L.num_pages = k_pool.size(0);
-    check_status(mg_paged_decode_plan(&L, seq_lens.data_ptr<int32_t>(), static_cast<int32_t>(B), with_staging ? 1 : 0,
+    check_status(mg_paged_decode_plan(&L, block_tables.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(),
+                                      static_cast<int32_t>(B), with_staging ? 1 : 0,
                                       plan.data_ptr(), plan.numel(), status_ptr(status), cur_stream()),
                  "decode_plan");
 }

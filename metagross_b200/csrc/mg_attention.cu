@@ -62,11 +62,11 @@ mg_status make_decode_plan(int kv4, int hd, int P, int Hkv, int Hq, int q_f16, i
                          G);
     }
     pl.ring = decode_ring(kv4 != 0, hd, pl.nt, pl.hpw, pl.nwarps);
-    // dynamic shared memory: [the CTA's plan records][head merge scratch][tail slots: warps x ring]
+    // dynamic shared memory: [the CTA's plan records, its first page ids][head merge scratch][tail slots: warps x ring]
     pl.grid = sm_count();
     const PlanLayout lay = plan_layout(batch, pl.grid);
     (void)lay;
-    const int64_t prefix_bytes = align_up(static_cast<int64_t>(kRecCache) * 32, 128);
+    const int64_t prefix_bytes = align_up(static_cast<int64_t>(kRecCache) * 32 + kPlanPids * 4, 128);
     const int ncols = pl.split_mode ? 1 : 2;
     const int64_t scratch_bytes =
         pl.wph > 1 ? align_up(static_cast<int64_t>(pl.nconsumers) * pl.nt * ncols * 4 * (hd + 2) * 4, 128) : 0;
@@ -125,7 +125,13 @@ void set_workspace(DecodeParams& p, const DecodePlan& pl, int Hq, int hd, void* 
 }
 
 mg_status launch(int kv4, int hd, const DecodeParams& p, const DecodePlan& pl, cudaStream_t s) {
-    return kv4 ? launch_decode_i4(p, pl, s, hd) : launch_decode_i8(p, pl, s, hd);
+    const bool p16 = p.P == 16;
+    if (kv4) {
+        if (hd == 64) return p16 ? launch_p<true, 64, true>(p, pl, s) : launch_p<true, 64, false>(p, pl, s);
+        return p16 ? launch_p<true, 128, true>(p, pl, s) : launch_p<true, 128, false>(p, pl, s);
+    }
+    if (hd == 64) return p16 ? launch_p<false, 64, true>(p, pl, s) : launch_p<false, 64, false>(p, pl, s);
+    return p16 ? launch_p<false, 128, true>(p, pl, s) : launch_p<false, 128, false>(p, pl, s);
 }
 
 bool aligned16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; }
@@ -191,7 +197,8 @@ extern "C" mg_status mg_paged_attention_committed(const float* query, const int8
     set_workspace(p, pl, static_cast<int>(num_q_heads), static_cast<int>(head_dim), workspace);
     // one sequence of num_blocks committed pages: plan it, then attend
     int32_t* plan = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + pl.plan_off);
-    st = launch_decode_plan(nullptr, static_cast<int32_t>(num_blocks * page_size), 1, static_cast<int>(page_size),
+    st = launch_decode_plan(block_table, nullptr, static_cast<int32_t>(num_blocks * page_size), 1,
+                            static_cast<int>(page_size),
                             p.max_blocks, 0, plan, pl.ws_bytes - pl.plan_off, dev_status, as_stream(stream));
     if (st != MG_OK) return st;
     p.plan = plan;
@@ -267,14 +274,14 @@ extern "C" int64_t mg_paged_decode_plan_bytes(int32_t batch) {
     return plan_layout(batch, sm_count()).words * 4;
 }
 
-extern "C" mg_status mg_paged_decode_plan(const mg_cache_layout* L, const int32_t* seq_lens, int32_t batch,
-                                          int32_t with_staging, void* plan, int64_t plan_bytes, int32_t* dev_status,
-                                          mg_stream_t stream) {
+extern "C" mg_status mg_paged_decode_plan(const mg_cache_layout* L, const int32_t* block_tables,
+                                          const int32_t* seq_lens, int32_t batch, int32_t with_staging, void* plan,
+                                          int64_t plan_bytes, int32_t* dev_status, mg_stream_t stream) {
     mg_status st = check_cache_layout(L);
     if (st != MG_OK) return st;
     MG_REQUIRE(batch >= 1 && batch <= kMaxBatch, "batch must be in [1, %d], got %d", kMaxBatch, batch);
-    MG_REQUIRE(seq_lens, "null pointer");
-    return launch_decode_plan(seq_lens, -1, batch, L->page_size, L->max_blocks, with_staging ? 1 : 0,
+    MG_REQUIRE(seq_lens && block_tables, "null pointer");
+    return launch_decode_plan(block_tables, seq_lens, -1, batch, L->page_size, L->max_blocks, with_staging ? 1 : 0,
                               static_cast<int32_t*>(plan), plan_bytes, dev_status, as_stream(stream));
 }
 
@@ -313,7 +320,7 @@ extern "C" mg_status mg_paged_decode_attention(const mg_cache_layout* L, const m
     MG_REQUIRE(workspace_bytes >= pl.ws_bytes, "workspace too small: %lld < %lld bytes", (long long)workspace_bytes,
                (long long)pl.ws_bytes);
     int32_t* plan = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + pl.plan_off);
-    st = launch_decode_plan(seq_lens, -1, batch, L->page_size, L->max_blocks, p.has_staging, plan,
+    st = launch_decode_plan(block_tables, seq_lens, -1, batch, L->page_size, L->max_blocks, p.has_staging, plan,
                             pl.ws_bytes - pl.plan_off, dev_status, as_stream(stream));
     if (st != MG_OK) return st;
     p.plan = plan;

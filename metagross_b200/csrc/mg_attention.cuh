@@ -75,20 +75,26 @@ __host__ __device__ constexpr int decode_ring(bool kv4, int hd, int nt, int hpw,
 //   [off_counts, +grid)  segments of each CTA
 //   [off_offs, +grid)    first record of each CTA in the flat array
 //   [off_recs, ...)      per CTA, its first kPlanInline records (one load)
+//   [off_pids, ...)      per CTA, the page ids of the first kPlanPids pages of its
+//                        first segment (block-table entries, so an attention
+//                        launch starts loading pages without that round trip)
 //   [off_flat, ...)      all records in CTA order, batch + grid at most
 //   [off_empty, +batch)  the sequences with nothing cached (outputs are zero)
 // A record is 8 words: {b, first page, pages, tail rows, partial slot (-1:
 // the whole sequence), first partial slot of b, pieces of b, 0}.
 constexpr int32_t kPlanMagic = 0x6d67706c;
+constexpr int kTailUnits = 2;     // work units the plan charges for a staged tail (a page is one)
 constexpr int kPlanInline = 4;    // records per CTA in the inline area
+constexpr int kPlanPids = 128;    // page ids per CTA in the plan
 constexpr int kRecCache = 64;     // records an attention CTA keeps in shared memory
 struct PlanLayout {
-    int off_counts, off_offs, off_recs, off_flat, off_empty;
+    int off_counts, off_offs, off_recs, off_pids, off_flat, off_empty;
     int64_t words;
 };
 PlanLayout plan_layout(int batch, int grid);
-mg_status launch_decode_plan(const int32_t* seq_lens, int32_t uniform_len, int batch, int P, int max_blocks,
-                             int has_staging, int32_t* plan, int64_t plan_bytes, int32_t* status, cudaStream_t s);
+mg_status launch_decode_plan(const int32_t* block_tables, const int32_t* seq_lens, int32_t uniform_len, int batch,
+                             int P, int max_blocks, int has_staging, int32_t* plan, int64_t plan_bytes,
+                             int32_t* status, cudaStream_t s);
 
 struct DecodeParams {
     const void* q;
@@ -282,12 +288,14 @@ struct TileRegs {
     uint32_t live;  // bit r: row g + 8r exists
 };
 
-// Page ids and scales of 32 upcoming pages of the warp's current segment,
-// lane i holding entry base + i (one shuffle per tile to read them).
+// Page ids of 32 upcoming pages of the warp's current segment, lane i
+// holding entry base + i (one shuffle per tile to read them).  spids: the
+// plan's copy of the first kPlanPids page ids of the CTA's first segment (in
+// shared memory), null for later segments, which read the block table.
 struct MetaCache {
     int base;
     int32_t pid;
-    float ks, vs;
+    const int32_t* spids;
 };
 
 template <bool KV4, int HD, int NT, bool SPLIT, bool P16, int HPW, int R, int NW>
@@ -295,7 +303,9 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
 
 mg_status make_decode_plan(int kv4, int hd, int P, int Hkv, int Hq, int q_f16, int batch, int staging_esize,
                            DecodePlan* out);
-mg_status launch_decode_i8(const DecodeParams& p, const DecodePlan& pl, cudaStream_t s, int hd);
-mg_status launch_decode_i4(const DecodeParams& p, const DecodePlan& pl, cudaStream_t s, int hd);
+// One kernel shape family (page format, head_dim, page size 16 or other); each is
+// instantiated in its own translation unit (mg_attn_<fmt>_d<hd>_<p16|pany>.cu).
+template <bool KV4, int HD, bool P16>
+mg_status launch_p(const DecodeParams& p, const DecodePlan& pl, cudaStream_t s);
 
 }  // namespace mg

@@ -263,9 +263,10 @@ __device__ __forceinline__ void attend_tail_chunk(HeadState<NT, HD / 16>& S, con
 
 // A piece of one sequence run by this CTA (one record of the decode plan),
 // and this warp's work items in it: its tiles (segment tiles wsub,
-// wsub + wph, ..., times the warp's heads), then its chunks of the staged
-// tail (rows wsub, wsub + wph, ..., up to tt rows per chunk, times the
-// warp's heads).
+// wsub + wph, ..., times the warp's heads) and its chunks of the staged tail
+// (rows wsub, wsub + wph, ..., up to tt rows per chunk, times the warp's
+// heads).  The tail chunks come first: their CUDA-core math then overlaps the
+// ramp of the page stream instead of trailing it.
 struct Segment {
     int b;
     int lo;      // first committed page of the segment (sequence-relative)
@@ -279,7 +280,8 @@ struct Segment {
     int ntile;   // the warp's tile items
     int ntt;     // the warp's tail rows (per head)
     int nchunk;  // its tail chunks (per head)
-    int nitems;  // ntile + nchunk * nh
+    int ntail;   // its tail items, nchunk * nh: items [0, ntail), its tiles after them
+    int nitems;  // ntail + ntile
 };
 
 __device__ __forceinline__ Segment make_segment(const int4* rec, int P, int wsub, int wph, int nh, int tt) {
@@ -299,7 +301,8 @@ __device__ __forceinline__ Segment make_segment(const int4* rec, int P, int wsub
     s.ntile = nloc * nh;
     s.ntt = wsub < s.tail ? (s.tail - 1 - wsub) / wph + 1 : 0;
     s.nchunk = (s.ntt + tt - 1) / tt;
-    s.nitems = s.ntile + s.nchunk * nh;
+    s.ntail = s.nchunk * nh;
+    s.nitems = s.ntail + s.ntile;
     return s;
 }
 
@@ -318,7 +321,7 @@ __device__ __forceinline__ void meta_refill(MetaCache& mc, const DecodeParams& p
     const int sp = P16 ? wsub + (base + lane) * wph : base + lane;
     int32_t pid = 0;
     if (sp < sg.npg) {
-        pid = row[sp];
+        pid = (mc.spids && sp < kPlanPids) ? mc.spids[sp] : row[sp];
         if (pid < 0 || pid >= p.num_pages) {
             flag(p.status, MG_DEV_BAD_PAGE_ID);
             pid = 0;
@@ -379,12 +382,14 @@ __device__ __forceinline__ void load_tile(TileRegs<KV4, HD>& T, MetaCache& mc, c
             ldg_words<C::VCHB>(vb + row * rs + g * C::VCHB, T.v[r]);
         }
         // L2 prefetch of the warp's tile kPrefetchTiles ahead: lane l brings K row l
-        // (l < 16) or V row l - 16 of this head, so the register ring reads from L2
+        // (l < 16) or V row l - 16 of this head, lanes 0 and 16 also the page's K / V
+        // scale, so the register ring reads from L2
         const int ja = jt + kPrefetchTiles;
         if (ja < nloc && ja < mc.base + kMetaLanes) {
             const int32_t pa = __shfl_sync(0xffffffffu, mc.pid, ja - mc.base);
             const uint8_t* pool = lane < 16 ? p.k_pool : p.v_pool;
             prefetch_l2(pool + static_cast<int64_t>(pa) * p.page_bytes + (lane & 15) * rs + h * C::ROWB);
+            if ((lane & 15) == 0) prefetch_l2((lane < 16 ? p.k_scales : p.v_scales) + pa);
         }
     } else {
         const int P = p.P;
@@ -558,6 +563,7 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
     float* mscratch = reinterpret_cast<float*>(smem + p.scratch_off);
     uint8_t* tslots = smem + p.tail_off + static_cast<int64_t>(warp) * R * p.tail_slot;
     int4* recs = reinterpret_cast<int4*>(smem);  // this CTA's segment records (plan)
+    int32_t* spids = reinterpret_cast<int32_t*>(smem + kRecCache * 32);  // first segment's page ids (plan)
 
     if (p.status && (*(volatile int32_t*)p.status & (MG_DEV_OUT_OF_PAGES | MG_DEV_BLOCK_TABLE_FULL))) return;
 
@@ -565,6 +571,8 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
     // round trip, more (stream-K over many short sequences) from the flat array --
     const int4* prec = reinterpret_cast<const int4*>(p.plan + p.lay.off_recs) + static_cast<int64_t>(cta) * kPlanInline * 2;
     if (tid < 2 * kPlanInline) recs[tid] = __ldcg(prec + tid);
+    const int4* ppid = reinterpret_cast<const int4*>(p.plan + p.lay.off_pids) + static_cast<int64_t>(cta) * (kPlanPids / 4);
+    if (tid >= 32 && tid < 32 + kPlanPids / 4) reinterpret_cast<int4*>(spids)[tid - 32] = __ldcg(ppid + tid - 32);
     if (tid == 0) {
         const bool ok = p.plan[0] == kPlanMagic && p.plan[1] == p.batch && p.plan[2] == static_cast<int>(gridDim.x) &&
                         p.plan[8] == p.has_staging;
@@ -619,6 +627,7 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
     int ji = 0;
     bool idone = false;
     mc.base = -(1 << 30);
+    mc.spids = spids;
     warm_segment<P16>(p, si, hbase, h1, HD, wsub, WPH, lane);
     // issue the next item of the walk into ring slot iphase; one cp.async
     // group per item (empty for tiles) keeps the group count in step
@@ -631,20 +640,22 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
                 si = make_segment(rec(sidx), p.P, wsub, WPH, nh, tt);
                 ji = 0;
                 mc.base = -(1 << 30);
+                mc.spids = nullptr;
                 warm_segment<P16>(p, si, hbase, h1, HD, wsub, WPH, lane);
             }
         }
         if (!idone) {
-            if (ji < si.ntile) {
-                const int hh = (si.nh == 2) ? (ji & 1) : 0;
-                const int jt = (si.nh == 2) ? (ji >> 1) : ji;
+            if (ji >= si.ntail) {
+                const int jj = ji - si.ntail;
+                const int hh = (si.nh == 2) ? (jj & 1) : 0;
+                const int jt = (si.nh == 2) ? (jj >> 1) : jj;
                 const int h = hh ? h1 : hbase;
                 const int nloc = si.nh == 2 ? (si.ntile >> 1) : si.ntile;
                 with_slot<R>(iphase, [&](auto k) {
                     load_tile<KV4, HD, P16>(tb[decltype(k)::value], mc, p, si, jt, nloc, h, wsub, WPH, g, c, lane);
                 });
             } else {
-                const int q = ji - si.ntile;
+                const int q = ji;
                 const int hh = q / si.nchunk, chunk = q - hh * si.nchunk;
                 const int n = min(tt, si.ntt - chunk * tt);
                 issue_tail_chunk(tslots + iphase * p.tail_slot, p, si.b, hh ? h1 : hbase, chunk, n, tt, hb, wsub,
@@ -657,13 +668,14 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
     };
     // the item in ring slot `phase`: one copy of the tile math, whatever the slot
     auto consume = [&](int phase, const Segment& sc, int j) {
-        if (j < sc.ntile) {
+        if (j >= sc.ntail) {
             TileRegs<KV4, HD> cur;
             with_slot<R>(phase, [&](auto k) { cur = tb[decltype(k)::value]; });
-            if (HPW == 2 && sc.nh == 2 && (j & 1)) attend_tile<KV4, HD, NT, SPLIT>(st[HPW - 1], cur, p.sm_scale_log2);
+            if (HPW == 2 && sc.nh == 2 && ((j - sc.ntail) & 1))
+                attend_tile<KV4, HD, NT, SPLIT>(st[HPW - 1], cur, p.sm_scale_log2);
             else attend_tile<KV4, HD, NT, SPLIT>(st[0], cur, p.sm_scale_log2);
         } else {
-            const int q = j - sc.ntile;
+            const int q = j;
             const int hh = q / sc.nchunk, chunk = q - hh * sc.nchunk;
             const int n = min(tt, sc.ntt - chunk * tt);
             cp_async_wait_group<R - 1>();
@@ -929,13 +941,6 @@ mg_status launch_p(const DecodeParams& p, const DecodePlan& pl, cudaStream_t s) 
     }
     if (pl.nt == 1) return launch_h<KV4, HD, 1, false, P16>(p, pl, s);
     return launch_h<KV4, HD, 2, false, P16>(p, pl, s);
-}
-
-template <bool KV4>
-mg_status launch_kv(const DecodeParams& p, const DecodePlan& pl, cudaStream_t s, int hd) {
-    const bool p16 = p.P == 16;
-    if (hd == 64) return p16 ? launch_p<KV4, 64, true>(p, pl, s) : launch_p<KV4, 64, false>(p, pl, s);
-    return p16 ? launch_p<KV4, 128, true>(p, pl, s) : launch_p<KV4, 128, false>(p, pl, s);
 }
 
 }  // namespace mg

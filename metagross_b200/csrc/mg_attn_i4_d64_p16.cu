@@ -1,0 +1,6 @@
+// Decode-attention kernel instantiations: packed-INT4 pages, head_dim 64, page size 16.
+#include "mg_attention_kernel.cuh"
+
+namespace mg {
+template mg_status launch_p<true, 64, true>(const DecodeParams&, const DecodePlan&, cudaStream_t);
+}  // namespace mg

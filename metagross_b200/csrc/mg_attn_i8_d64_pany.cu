@@ -1,0 +1,6 @@
+// Decode-attention kernel instantiations: INT8 pages, head_dim 64, any other page size.
+#include "mg_attention_kernel.cuh"
+
+namespace mg {
+template mg_status launch_p<false, 64, false>(const DecodeParams&, const DecodePlan&, cudaStream_t);
+}  // namespace mg

@@ -3,8 +3,11 @@
 // (and the page size), which every layer of a decode step shares, so one
 // plan serves all the step's attention launches.
 //
-// Work is counted in "units": one committed page, or the staged tail (< P
-// rows), of one sequence.  Two partitions:
+// Work is counted in "units": one committed page is one unit, the staged
+// tail (< P exact rows, folded in on the CUDA cores) of a sequence is
+// kTailUnits units, about what it costs next to a page.  A piece of the
+// tail's weight that falls into another CTA's range is an empty piece (no
+// pages, no tail; it merges as a zero partial).  Two partitions:
 //   chunk     when the non-empty sequences fit on the SMs: each sequence gets
 //             k_b = ceil(U_b / S) near-equal chunks with S the smallest chunk
 //             size for which sum_b k_b <= #CTAs (so the longest chunk is as
@@ -24,6 +27,7 @@ namespace {
 constexpr int kPlanThreads = 1024;
 
 struct PlanParams {
+    const int32_t* block_tables;  // [batch, max_blocks]
     const int32_t* seq_lens;
     int32_t uniform_len;  // >= 0: every sequence has this many committed tokens
     int batch, P, max_blocks, has_staging;
@@ -95,6 +99,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) decode_plan_kernel(const Plan
     int* aux = pre + B + 1;     // [B + 1] chunks per sequence / pieces per sequence, then their prefix
     int* aux2 = aux + B + 1;    // [B + 1] partial-slot prefix
     int* tmp = aux2 + B + 1;    // [max(B, 2 * grid + 1)]
+    int* first = tmp + (B > 2 * G + 1 ? B : 2 * G + 1);  // [3 * grid]: (b, lo, npg) of each CTA's first segment
 
     // ---- lengths and units --------------------------------------------------------
     int nonempty = 0, maxu = 0;
@@ -110,7 +115,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) decode_plan_kernel(const Plan
             }
         }
         const int np = l / P;
-        const int u = np + ((pp.has_staging && l - np * P > 0) ? 1 : 0);
+        const int u = np + ((pp.has_staging && l - np * P > 0) ? kTailUnits : 0);
         len[b] = l;
         units[b] = u;
         nonempty += u > 0;
@@ -160,6 +165,9 @@ __global__ void __launch_bounds__(kPlanThreads, 1) decode_plan_kernel(const Plan
                 const int tail = (uhi == u && tb > 0) ? tb : 0;
                 const int cta = aux[b] + j;
                 write_rec(pp, cta, cta, 0, b, ulo, npg, tail, k > 1 ? aux2[b] + j : -1, aux2[b], k);
+                first[3 * cta] = b;
+                first[3 * cta + 1] = ulo;
+                first[3 * cta + 2] = npg;
                 pp.plan[pp.lay.off_counts + cta] = 1;
                 pp.plan[pp.lay.off_offs + cta] = cta;
             }
@@ -206,6 +214,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) decode_plan_kernel(const Plan
         __syncthreads();
         block_scan_array(tmp, tmp + G, G, scratch);  // tmp[G..2G]: flat offsets
         const int* offs = tmp + G;
+        int* firstseg = first;
         for (int c = threadIdx.x; c < GR; c += blockDim.x) {
             const int64_t u0 = static_cast<int64_t>(c) * W / GR, u1 = static_cast<int64_t>(c + 1) * W / GR;
             int k = 0;
@@ -221,13 +230,31 @@ __global__ void __launch_bounds__(kPlanThreads, 1) decode_plan_kernel(const Plan
                 const bool whole = lo == 0 && hi == ue - ub;
                 const int first = cta_of_unit(ub);
                 write_rec(pp, c, offs[c], k, b, lo, npg, tail, whole ? -1 : aux2[b] + (c - first), aux2[b], aux[b]);
+                if (k == 0) {
+                    firstseg[3 * c] = b;
+                    firstseg[3 * c + 1] = lo;
+                    firstseg[3 * c + 2] = npg;
+                }
                 ++k;
             }
             pp.plan[pp.lay.off_counts + c] = k;
             pp.plan[pp.lay.off_offs + c] = offs[c];
         }
     }
-    for (int c = used + threadIdx.x; c < G; c += blockDim.x) pp.plan[pp.lay.off_counts + c] = 0;
+    for (int c = used + threadIdx.x; c < G; c += blockDim.x) {
+        pp.plan[pp.lay.off_counts + c] = 0;
+        first[3 * c + 2] = 0;
+    }
+    __syncthreads();
+    // ---- page ids of each CTA's first kPlanPids pages (its first segment), so an
+    // attention launch starts loading pages without a block-table round trip ------
+    for (int i = threadIdx.x; i < G * kPlanPids; i += blockDim.x) {
+        const int c = i / kPlanPids, k = i - c * kPlanPids;
+        int32_t pid = 0;
+        if (k < first[3 * c + 2])
+            pid = pp.block_tables[static_cast<int64_t>(first[3 * c]) * pp.max_blocks + first[3 * c + 1] + k];
+        pp.plan[pp.lay.off_pids + i] = pid;
+    }
     if (threadIdx.x == 0) {
         int32_t* h = pp.plan;
         h[0] = kPlanMagic;
@@ -249,20 +276,23 @@ PlanLayout plan_layout(int batch, int grid) {
     L.off_counts = 16;
     L.off_offs = L.off_counts + grid;
     L.off_recs = ((L.off_offs + grid) + 7) / 8 * 8;
-    L.off_flat = L.off_recs + grid * kPlanInline * 8;
+    L.off_pids = L.off_recs + grid * kPlanInline * 8;
+    L.off_flat = L.off_pids + grid * kPlanPids;
     L.off_empty = L.off_flat + (batch + grid) * 8;
     L.words = L.off_empty + batch;
     return L;
 }
 
-mg_status launch_decode_plan(const int32_t* seq_lens, int32_t uniform_len, int batch, int P, int max_blocks,
-                             int has_staging, int32_t* plan, int64_t plan_bytes, int32_t* status, cudaStream_t s) {
+mg_status launch_decode_plan(const int32_t* block_tables, const int32_t* seq_lens, int32_t uniform_len, int batch,
+                             int P, int max_blocks, int has_staging, int32_t* plan, int64_t plan_bytes,
+                             int32_t* status, cudaStream_t s) {
     const int G = sm_count();
     const PlanLayout lay = plan_layout(batch, G);
     MG_REQUIRE(plan && plan_bytes >= static_cast<int64_t>(lay.words) * 4, "decode plan buffer too small: %lld < %lld",
                (long long)plan_bytes, (long long)lay.words * 4);
     MG_REQUIRE((reinterpret_cast<uintptr_t>(plan) & 15u) == 0, "decode plan buffer must be 16-byte aligned");
     PlanParams pp{};
+    pp.block_tables = block_tables;
     pp.seq_lens = seq_lens;
     pp.uniform_len = uniform_len;
     pp.batch = batch;
@@ -273,7 +303,8 @@ mg_status launch_decode_plan(const int32_t* seq_lens, int32_t uniform_len, int b
     pp.lay = lay;
     pp.plan = plan;
     pp.status = status;
-    const size_t smem = (static_cast<size_t>(6) * batch + 3 + 2 * G + 1) * sizeof(int);
+    const size_t tmp_ints = static_cast<size_t>(batch > 2 * G + 1 ? batch : 2 * G + 1);
+    const size_t smem = (static_cast<size_t>(5) * batch + 3 + tmp_ints + 3 * static_cast<size_t>(G)) * sizeof(int);
     static int64_t attr_set[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);

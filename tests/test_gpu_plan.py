@@ -21,23 +21,26 @@ def _C():
 
 
 INLINE = 4
+PIDS = 128  # page ids of each CTA's first segment kept in the plan
+TAIL_UNITS = 2  # a staged tail weighs two units in the partition
 
 
 def layout(batch, grid):
     off_counts = 16
     off_offs = off_counts + grid
     off_recs = (off_offs + grid + 7) // 8 * 8
-    off_flat = off_recs + grid * INLINE * 8
+    off_pids = off_recs + grid * INLINE * 8
+    off_flat = off_pids + grid * PIDS
     off_empty = off_flat + (batch + grid) * 8
-    return off_counts, off_offs, off_recs, off_flat, off_empty
+    return off_counts, off_offs, off_recs, off_pids, off_flat, off_empty
 
 
 def plan_ref(lens, P, max_blocks, has_staging, G):
     """Plain-Python statement of the partition (mirrors mg_plan.cu)."""
     B = len(lens)
-    off_counts, off_offs, off_recs, off_flat, off_empty = layout(B, G)
+    off_counts, off_offs, off_recs, off_pids, off_flat, off_empty = layout(B, G)
     lens = [l if (0 <= l and l // P <= max_blocks) else 0 for l in lens]
-    units = [l // P + (1 if has_staging and l % P else 0) for l in lens]
+    units = [l // P + (TAIL_UNITS if has_staging and l % P else 0) for l in lens]
     pre = np.concatenate([[0], np.cumsum(units)]).astype(np.int64)
     W = int(pre[-1])
     counts = [0] * G
@@ -103,8 +106,8 @@ def plan_ref(lens, P, max_blocks, has_staging, G):
                     kk += 1
                 b += 1
             counts[c] = kk
-    return dict(off_offs=off_offs, off_recs=off_recs, off_flat=off_flat, off_empty=off_empty, counts=counts, recs=recs,
-                empties=empties, mode=1 if chunk else 2, W=W, used=used)
+    return dict(off_offs=off_offs, off_recs=off_recs, off_pids=off_pids, off_flat=off_flat, off_empty=off_empty,
+                counts=counts, recs=recs, empties=empties, mode=1 if chunk else 2, W=W, used=used)
 
 
 def build_plan(lens, P=16, max_blocks=None, has_staging=True):
@@ -112,16 +115,17 @@ def build_plan(lens, P=16, max_blocks=None, has_staging=True):
     B = len(lens)
     max_blocks = max_blocks or max(1, max(lens) // P + 1)
     k_pool = torch.zeros(1, P, 1, 64, dtype=torch.int8, device="cuda")
-    bt = torch.zeros(B, max_blocks, dtype=torch.int32, device="cuda")
+    bt = torch.randint(0, 1 << 20, (B, max_blocks), generator=torch.Generator().manual_seed(B),
+                       dtype=torch.int32).cuda()
     sl = torch.tensor(lens, dtype=torch.int32, device="cuda")
     plan = torch.zeros(C.decode_plan_bytes(B), dtype=torch.uint8, device="cuda")
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     C.decode_plan(k_pool, bt, sl, has_staging, plan, status)
     words = plan.view(torch.int32).cpu().numpy()
-    return words, int(status.item()), max_blocks
+    return words, int(status.item()), max_blocks, bt.cpu().numpy()
 
 
-def check(words, ref, lens, P, has_staging, G):
+def check(words, ref, lens, P, has_staging, G, bt=None):
     B = len(lens)
     assert words[0] == MAGIC and words[1] == B and words[2] == G
     assert words[4] == len(ref["empties"]) and words[5] == ref["mode"] and words[6] == ref["W"]
@@ -138,6 +142,15 @@ def check(words, ref, lens, P, has_staging, G):
             o = ref["off_recs"] + (c * INLINE + k) * 8
             assert tuple(words[o:o + 8].tolist()) == rec, (c, k, "inline")
     assert sorted(words[ref["off_empty"]:ref["off_empty"] + len(ref["empties"])].tolist()) == ref["empties"]
+    # page ids of each CTA's first segment, copied from the block table
+    if bt is not None:
+        for c in range(G):
+            want = np.zeros(PIDS, dtype=np.int64)
+            if counts[c] > 0:
+                b, lo, npg = ref["recs"][(c, 0)][:3]
+                n = min(npg, PIDS)
+                want[:n] = bt[b, lo:lo + n]
+            np.testing.assert_array_equal(words[ref["off_pids"] + c * PIDS:ref["off_pids"] + (c + 1) * PIDS], want)
     # invariants: every unit covered once, partial slots distinct per sequence
     cover = {b: [] for b in range(B)}
     slots = set()
@@ -187,16 +200,16 @@ def test_plan_matches_restatement(case):
         lens = g.lognormal(np.log(2048), 0.8, 1024).clip(1, 32768).astype(int).tolist()
     else:
         lens = [0, 0, 0]
-    words, status, max_blocks = build_plan(lens, has_staging=has_staging)
+    words, status, max_blocks, bt = build_plan(lens, has_staging=has_staging)
     assert status == 0
     ref = plan_ref(lens, 16, max_blocks, has_staging, G)
-    check(words, ref, lens, 16, has_staging, G)
+    check(words, ref, lens, 16, has_staging, G, bt)
 
 
 def test_plan_flags_bad_lengths():
     G = _grid()
     lens = [40, -3, 16 * 100]  # max_blocks 4: the last is too long, -3 negative
-    words, status, max_blocks = build_plan(lens, max_blocks=4)
+    words, status, max_blocks, bt = build_plan(lens, max_blocks=4)
     assert status & 0x80
     ref = plan_ref(lens, 16, 4, True, G)
-    check(words, ref, [40, 0, 0], 16, True, G)
+    check(words, ref, [40, 0, 0], 16, True, G, bt)
