@@ -59,6 +59,12 @@ typedef enum mg_status {
 #define MG_DEV_BAD_ARGUMENT 0x80     /* a per-sequence argument (n_new > max_new, seq id, cu_seqlens) was inconsistent; that sequence was skipped */
 
 typedef enum mg_kv_dtype { MG_KV_INT8 = 0, MG_KV_INT4 = 1 } mg_kv_dtype;
+/* Scale granularity of a batched pool.  MG_SCALE_PAGE is the reference's only
+ * layout (metagross/cache.py:39,69-70: one fp32 per physical page, K and V
+ * separately).  MG_SCALE_TOKEN_HEAD has no counterpart in the reference: one
+ * fp32 absmax scale per (page, token, kv head), each D-vector quantized as the
+ * reference's quantize_new_scale quantizes a [1, 1, D] slice. */
+typedef enum mg_scale_layout { MG_SCALE_PAGE = 0, MG_SCALE_TOKEN_HEAD = 1 } mg_scale_layout;
 typedef enum mg_float_dtype { MG_F32 = 0, MG_F16 = 1 } mg_float_dtype;
 
 MG_API const char* mg_version(void);
@@ -145,14 +151,16 @@ typedef struct mg_cache_layout {
     int32_t head_dim;      /* D: 64 or 128 for attention; the quantize/dequantize kernels take any even D with D*bits/8 % 16 == 0 */
     int32_t max_blocks;    /* width of a block-table row */
     int64_t num_pages;     /* pool capacity N */
+    int32_t scale_layout;  /* mg_scale_layout; MG_SCALE_TOKEN_HEAD needs head_dim a power of two <= 256 */
+    int32_t reserved;      /* 0 */
 } mg_cache_layout;
 
 /* Device pointers of one layer. */
 typedef struct mg_layer_ptrs {
     void* k_pool;    /* [N, P, Hkv, D] int8 or [N, P, Hkv, D/2] uint8 */
     void* v_pool;
-    float* k_scales; /* [N] */
-    float* v_scales; /* [N] */
+    float* k_scales; /* [N] (MG_SCALE_PAGE) or [N, P, Hkv] (MG_SCALE_TOKEN_HEAD) */
+    float* v_scales; /* same shape as k_scales */
     void* staging_k; /* [B, P, Hkv, D] staging_dtype: tokens of the page being filled */
     void* staging_v;
 } mg_layer_ptrs;
@@ -186,8 +194,9 @@ MG_API mg_status mg_plan_append(const mg_allocator* alloc, int32_t* block_tables
  * [batch, max_new, Hkv, D] in new_dtype (f16 or f32); seq_lens are the lengths
  * AFTER the step, n_new the tokens added.  A page that fills is quantized with
  * one fresh absmax scale over the whole page (K and V separately) exactly as
- * metagross/cache.py:63-72 + csrc/quantize.cu; the partial page's tokens go
- * to staging unquantized. */
+ * metagross/cache.py:63-72 + csrc/quantize.cu; with MG_SCALE_TOKEN_HEAD every
+ * (token, head) D-vector of the page gets its own fresh absmax scale.  The
+ * partial page's tokens go to staging unquantized. */
 MG_API mg_status mg_kv_append(const mg_cache_layout* layout, const mg_layer_ptrs* layer,
                        const int32_t* block_tables, const int32_t* seq_lens, const int32_t* n_new,
                        int32_t batch, const void* k_new, const void* v_new, int32_t new_dtype,

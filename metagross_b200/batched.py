@@ -7,7 +7,9 @@ every piece of state in device memory and no host synchronisation per step.
 
 State (per cache):
   k_pool, v_pool   [L, N, P, Hkv, D] int8  or [L, N, P, Hkv, D/2] uint8 (INT4)
-  k_scales, v_scales [L, N] fp32, one scale per physical page
+  k_scales, v_scales [L, N] fp32, one scale per physical page (the
+                   reference's layout), or with scale_granularity="token_head"
+                   [L, N, P, Hkv]: one absmax scale per token and kv head
   staging_k/v      [L, B, P, Hkv, D] (fp16 or fp32): the page being filled,
                    exact, never quantized
   block_tables     [B, max_blocks] int32, shared by all layers (every layer
@@ -56,9 +58,13 @@ def _get_C():
 
 class BatchedPagedKVCache:
     def __init__(self, num_layers, batch, num_kv_heads, head_dim, page_size=16, num_pages=None, max_blocks=None,
-                 kv_dtype="int8", staging_dtype=torch.float16, device="cuda"):
+                 kv_dtype="int8", staging_dtype=torch.float16, device="cuda", scale_granularity="page"):
         if kv_dtype not in ("int8", "int4"):
             raise ValueError(f"kv_dtype must be 'int8' or 'int4', got {kv_dtype!r}")
+        if scale_granularity not in ("page", "token_head"):
+            raise ValueError(f"scale_granularity must be 'page' or 'token_head', got {scale_granularity!r}")
+        if scale_granularity == "token_head" and (head_dim > 256 or head_dim & (head_dim - 1)):
+            raise ValueError("token_head scales need head_dim a power of two <= 256")
         for name, v in (("num_layers", num_layers), ("batch", batch), ("num_kv_heads", num_kv_heads),
                         ("head_dim", head_dim), ("page_size", page_size)):
             if v <= 0:
@@ -70,6 +76,7 @@ class BatchedPagedKVCache:
         self.num_layers, self.batch = num_layers, batch
         self.num_kv_heads, self.head_dim, self.page_size = num_kv_heads, head_dim, page_size
         self.kv_dtype = kv_dtype
+        self.scale_granularity = scale_granularity
         self.staging_dtype = staging_dtype
         self.device = torch.device(device)
         self.max_blocks = int(max_blocks) if max_blocks else 64
@@ -79,7 +86,8 @@ class BatchedPagedKVCache:
         shape = (num_layers, self.num_pages, page_size, num_kv_heads, row)
         self.k_pool = torch.zeros(shape, dtype=dt, device=self.device)
         self.v_pool = torch.zeros(shape, dtype=dt, device=self.device)
-        self.k_scales = torch.zeros(num_layers, self.num_pages, dtype=torch.float32, device=self.device)
+        sshape = (num_layers, self.num_pages) + ((page_size, num_kv_heads) if scale_granularity == "token_head" else ())
+        self.k_scales = torch.zeros(sshape, dtype=torch.float32, device=self.device)
         self.v_scales = torch.zeros_like(self.k_scales)
         st = (num_layers, batch, page_size, num_kv_heads, head_dim)
         self.staging_k = torch.zeros(st, dtype=staging_dtype, device=self.device)
@@ -227,6 +235,7 @@ class BatchedPagedKVCache:
             raise RuntimeError(f"paged KV cache device error 0x{s:x}: {', '.join(names)}")
 
     def memory_bytes(self) -> int:
+        """Bytes of the quantized pools (codes only, as the reference's LayerKVCache.memory_bytes)."""
         return self.k_pool.numel() + self.v_pool.numel()
 
 

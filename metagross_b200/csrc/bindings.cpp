@@ -268,10 +268,14 @@ Pools make_pools(const torch::Tensor& k_pool, const torch::Tensor& v_pool, const
     const bool i4 = k_pool.scalar_type() == torch::kUInt8;
     TORCH_CHECK(i4 || k_pool.scalar_type() == torch::kInt8, "pools must be int8 (INT8) or uint8 (packed INT4)");
     TORCH_CHECK(v_pool.scalar_type() == k_pool.scalar_type(), "k_pool and v_pool dtypes differ");
+    // scales [N]: one per page (the reference's layout); [N, P, Hkv]: one per token and kv head
+    const bool th = k_scales.dim() == 3;
     TORCH_CHECK(k_scales.scalar_type() == torch::kFloat32 && v_scales.scalar_type() == torch::kFloat32 &&
-                    k_scales.is_contiguous() && v_scales.is_contiguous() && k_scales.numel() == k_pool.size(0) &&
-                    v_scales.numel() == k_pool.size(0),
-                "k_scales/v_scales must be contiguous float32 [num_pages]");
+                    k_scales.is_contiguous() && v_scales.is_contiguous() && v_scales.sizes() == k_scales.sizes() &&
+                    (th ? (k_scales.size(0) == k_pool.size(0) && k_scales.size(1) == k_pool.size(1) &&
+                           k_scales.size(2) == k_pool.size(2))
+                        : (k_scales.dim() == 1 && k_scales.size(0) == k_pool.size(0))),
+                "k_scales/v_scales must be contiguous float32 [num_pages] or [num_pages, page_size, num_kv_heads]");
     TORCH_CHECK(block_tables.is_cuda() && block_tables.scalar_type() == torch::kInt32 && block_tables.dim() == 2 &&
                     block_tables.is_contiguous(),
                 "block_tables must be a contiguous CUDA int32 [batch, max_blocks] tensor");
@@ -282,6 +286,7 @@ Pools make_pools(const torch::Tensor& k_pool, const torch::Tensor& v_pool, const
     p.L.head_dim = static_cast<int32_t>(i4 ? k_pool.size(3) * 2 : k_pool.size(3));
     p.L.max_blocks = static_cast<int32_t>(block_tables.size(1));
     p.L.num_pages = k_pool.size(0);
+    p.L.scale_layout = th ? MG_SCALE_TOKEN_HEAD : MG_SCALE_PAGE;
     p.L.staging_dtype = MG_F32;
     p.ptrs.k_pool = k_pool.data_ptr();
     p.ptrs.v_pool = v_pool.data_ptr();

@@ -34,9 +34,10 @@ mg_status make_decode_plan(int kv4, int hd, int P, int Hkv, int Hq, int q_f16, i
     if (pl.nt > 2) return set_error(MG_ERR_UNSUPPORTED, "GQA group %d too large (fp32 q: <= 8, fp16 q: <= 16)", G);
     // warps: one kv head each, several warps per head when there are few kv
     // heads, two heads per warp (head_dim 64, one n-tile) beyond that.  Head
-    // dim 64 with one n-tile picks 12 warps (deep ring) or 16 (more warps) by
-    // the bytes each SM keeps in flight; the register-heavy shapes (head_dim
-    // 128, two n-tiles) run 8 wide warps when there are at most 8 kv heads.
+    // dim 64 with one n-tile picks 12 or 16 warps by the bytes each SM keeps
+    // in flight (warps with a head x (ring - 1) tiles; 12 on a tie); the
+    // register-heavy shapes (head_dim 128, two n-tiles) run 8 wide warps when
+    // there are at most 8 kv heads.
     const bool light = hd == 64 && pl.nt == 1;
     const int tile_bytes = 16 * (kv4 ? hd / 2 : hd);
     if (light && Hkv <= kWarps) {
@@ -125,7 +126,9 @@ void set_workspace(DecodeParams& p, const DecodePlan& pl, int Hq, int hd, void* 
 }
 
 mg_status launch(int kv4, int hd, const DecodeParams& p, const DecodePlan& pl, cudaStream_t s) {
-    const bool p16 = p.P == 16;
+    // the 16-token-page kernels read one scale per tile; per-token scales take
+    // the general path, which looks up each row's page and scale
+    const bool p16 = p.P == 16 && !p.scale_th;
     if (kv4) {
         if (hd == 64) return p16 ? launch_p<true, 64, true>(p, pl, s) : launch_p<true, 64, false>(p, pl, s);
         return p16 ? launch_p<true, 128, true>(p, pl, s) : launch_p<true, 128, false>(p, pl, s);
@@ -248,6 +251,7 @@ mg_status prepare_batched(const mg_cache_layout* L, const mg_layer_ptrs* lp, con
     p.v_pool = static_cast<const uint8_t*>(lp->v_pool);
     p.k_scales = lp->k_scales;
     p.v_scales = lp->v_scales;
+    p.scale_th = L->scale_layout == MG_SCALE_TOKEN_HEAD;
     p.staging_k = lp->staging_k;
     p.staging_v = lp->staging_v;
     p.st_f16 = L->staging_dtype == MG_F16;

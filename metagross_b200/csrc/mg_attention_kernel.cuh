@@ -9,7 +9,7 @@ namespace mg {
 // One 16-token tile of one kv head, already in registers: S^T = K Q^T on the
 // tensor cores, online softmax update, O^T += V^T P^T.  sscale: softmax scale
 // times log2(e).
-template <bool KV4, int HD, int NT, bool SPLIT>
+template <bool KV4, int HD, int NT, bool SPLIT, bool P16>
 __device__ __forceinline__ void attend_tile(HeadState<NT, HD / 16>& S, const TileRegs<KV4, HD>& T, float sscale) {
     using C = Cfg<KV4, HD, NT>;
     constexpr int NCOLS = SPLIT ? 1 : 2;
@@ -32,8 +32,9 @@ __device__ __forceinline__ void attend_tile(HeadState<NT, HD / 16>& S, const Til
             else mma_16816(sc[nt], a, S.qf[nt][kk][0], S.qf[nt][kk][1]);
         }
     }
-    const float ks0 = T.ks[0] * sscale, ks1 = T.ks[1] * sscale;
-    const float vs0 = T.vs[0], vs1 = T.vs[1];
+    // page size 16 (page scales): one page per tile, its scales live in slot 0 only
+    const float ks0 = T.ks[0] * sscale, ks1 = T.ks[P16 ? 0 : 1] * sscale;
+    const float vs0 = T.vs[0], vs1 = T.vs[P16 ? 0 : 1];
 
     // ---- online softmax (log2 domain, lazy rescale) ---------------------------------
     float s[NT][NCOLS][2];
@@ -366,10 +367,10 @@ __device__ __forceinline__ void load_tile(TileRegs<KV4, HD>& T, MetaCache& mc, c
     if (P16) {
         if (jt >= mc.base + kMetaLanes) meta_refill<true>(mc, p, sg, jt, wsub, wph, lane);
         const int32_t pid = __shfl_sync(0xffffffffu, mc.pid, jt - mc.base);
-        const float ks = __ldg(p.k_scales + pid);
-        const float vs = __ldg(p.v_scales + pid);
-        T.ks[0] = T.ks[1] = ks;
-        T.vs[0] = T.vs[1] = vs;
+        // scales straight into slot 0 (attend_tile reads slot 0 for both rows): a
+        // copy of a load still in flight would stall the issuing warp
+        T.ks[0] = __ldg(p.k_scales + pid);
+        T.vs[0] = __ldg(p.v_scales + pid);
         T.live = 3u;
         const int64_t off = static_cast<int64_t>(pid) * p.page_bytes + h * C::ROWB;
         const uint8_t* kb = p.k_pool + off;
@@ -410,8 +411,9 @@ __device__ __forceinline__ void load_tile(TileRegs<KV4, HD>& T, MetaCache& mc, c
             const int dp = static_cast<int>(p.pdiv.div(static_cast<uint32_t>(rel)));
             const int tok = rel - dp * P;
             const int32_t pid = __shfl_sync(0xffffffffu, mc.pid, pfirst + dp - mc.base);
-            T.ks[r] = __ldg(p.k_scales + pid);
-            T.vs[r] = __ldg(p.v_scales + pid);
+            const int64_t si = p.scale_th ? (static_cast<int64_t>(pid) * P + tok) * p.Hkv + h : pid;
+            T.ks[r] = __ldg(p.k_scales + si);
+            T.vs[r] = __ldg(p.v_scales + si);
             T.live |= live ? (1u << r) : 0u;
             ldg_words<C::KCHB>(p.k_pool + static_cast<int64_t>(pid) * p.page_bytes + tok * rs + h * C::ROWB +
                                    c * C::KCHB,
@@ -666,14 +668,24 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
         cp_async_commit();
         iphase = (iphase + 1 == R) ? 0 : iphase + 1;
     };
-    // the item in ring slot `phase`: one copy of the tile math, whatever the slot
+    // the item in ring slot `phase`.  A ring of two with registers to spare
+    // (12 warps, 168 each) keeps one copy of the tile math per slot and no
+    // register copy; otherwise the slot is copied into one copy of the math,
+    // which keeps the kernel inside the instruction cache and the register file
     auto consume = [&](int phase, const Segment& sc, int j) {
         if (j >= sc.ntail) {
-            TileRegs<KV4, HD> cur;
-            with_slot<R>(phase, [&](auto k) { cur = tb[decltype(k)::value]; });
-            if (HPW == 2 && sc.nh == 2 && ((j - sc.ntail) & 1))
-                attend_tile<KV4, HD, NT, SPLIT>(st[HPW - 1], cur, p.sm_scale_log2);
-            else attend_tile<KV4, HD, NT, SPLIT>(st[0], cur, p.sm_scale_log2);
+            const bool second = HPW == 2 && sc.nh == 2 && ((j - sc.ntail) & 1);
+            if constexpr (R <= 2 && NW <= kWarpsDeep) {
+                with_slot<R>(phase, [&](auto k) {
+                    if (second) attend_tile<KV4, HD, NT, SPLIT, P16>(st[HPW - 1], tb[decltype(k)::value], p.sm_scale_log2);
+                    else attend_tile<KV4, HD, NT, SPLIT, P16>(st[0], tb[decltype(k)::value], p.sm_scale_log2);
+                });
+            } else {
+                TileRegs<KV4, HD> cur;
+                with_slot<R>(phase, [&](auto k) { cur = tb[decltype(k)::value]; });
+                if (second) attend_tile<KV4, HD, NT, SPLIT, P16>(st[HPW - 1], cur, p.sm_scale_log2);
+                else attend_tile<KV4, HD, NT, SPLIT, P16>(st[0], cur, p.sm_scale_log2);
+            }
         } else {
             const int q = j;
             const int hh = q / sc.nchunk, chunk = q - hh * sc.nchunk;

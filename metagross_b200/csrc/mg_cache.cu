@@ -198,9 +198,31 @@ struct AppendParams {
     const int32_t* n_new;
     int32_t P;
     int32_t row;  // Hkv * D elements per token
+    int32_t D;
+    int32_t scale_th;  // scales [N, P, Hkv] (one per token and head) instead of [N]
     int64_t num_pages;
     int32_t* status;
 };
+
+// Code of 8 consecutive elements into the pool at element e of a page (INT8:
+// 8 bytes, INT4: 4 bytes of nibbles, the even element in the low nibble).
+template <bool INT4>
+__device__ __forceinline__ void store_codes(uint8_t* page_base, int64_t e, const float (&v)[8], float sf) {
+    if (!INT4) {
+        uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            w0 |= (static_cast<uint32_t>(quant_code(v[i], sf, 127.0f)) & 0xFFu) << (8 * i);
+            w1 |= (static_cast<uint32_t>(quant_code(v[4 + i], sf, 127.0f)) & 0xFFu) << (8 * i);
+        }
+        *reinterpret_cast<uint2*>(page_base + e) = make_uint2(w0, w1);
+    } else {
+        uint32_t w = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w |= (static_cast<uint32_t>(quant_code(v[i], sf, 7.0f)) & 0xFu) << (4 * i);
+        *reinterpret_cast<uint32_t*>(page_base + e / 2) = w;
+    }
+}
 
 template <bool INT4, typename ST, typename NT>
 __global__ void __launch_bounds__(kAppendThreads) kv_append_kernel(AppendParams p) {
@@ -225,8 +247,41 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_kernel(AppendParams 
 
     if (page_start + P <= new_len) {  // page j fills during this step: commit it
         const int32_t page = j < p.max_blocks ? p.block_tables[static_cast<int64_t>(b) * p.max_blocks + j] : -1;
+        uint8_t* pool = static_cast<uint8_t*>(kv ? p.v_pool : p.k_pool);
+        float* scales = kv ? p.v_scales : p.k_scales;
         if (page < 0 || page >= p.num_pages) {
             if (threadIdx.x == 0) flag(p.status, MG_DEV_BAD_PAGE_ID);
+        } else if (p.scale_th) {
+            // one fresh scale per (token, head) D-vector, the reference's
+            // quantize_new_scale of a [1, 1, D] slice: the D / 8 consecutive
+            // threads holding a vector reduce its absmax by shuffles (every
+            // thread runs every round, so the shuffles never diverge)
+            const int gl = p.D >> 3;
+            uint8_t* base = pool + static_cast<int64_t>(page) * (INT4 ? pe / 2 : pe);
+            for (int64_t r0 = 0; r0 < pe; r0 += kAppendThreads * 8) {
+                const int64_t e = r0 + threadIdx.x * 8;
+                const bool ok = e < pe;
+                const int t = ok ? static_cast<int>(e / row) : 0;
+                const int tok = page_start + t;
+                const int64_t c = e - static_cast<int64_t>(t) * row;
+                float v[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+                if (ok) {
+                    if (tok < old) Vec8<ST>::load(staging + static_cast<int64_t>(t) * row + c, v);
+                    else Vec8<NT>::load(src_new + static_cast<int64_t>(tok - old) * row + c, v);
+                }
+                float a = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) a = fmaxf(a, fabsf(v[i]));
+                for (int o = gl >> 1; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+                if (ok) {
+                    const float sf = static_cast<float>(scale_from_absmax(a, INT4 ? 7.0 : 127.0));
+                    if ((threadIdx.x & (gl - 1)) == 0)
+                        scales[(static_cast<int64_t>(page) * P + t) * (row / p.D) + c / p.D] = sf;
+                    store_codes<INT4>(base, e, v, sf);
+                }
+            }
         } else {
             // element e of the page: token t = e / row
             float a = 0.0f;
@@ -243,8 +298,8 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_kernel(AppendParams 
             a = block_max(a, red);
             const double s = scale_from_absmax(a, INT4 ? 7.0 : 127.0);
             const float sf = static_cast<float>(s);
-            if (threadIdx.x == 0) (kv ? p.v_scales : p.k_scales)[page] = sf;
-            uint8_t* pool = static_cast<uint8_t*>(kv ? p.v_pool : p.k_pool);
+            if (threadIdx.x == 0) scales[page] = sf;
+            uint8_t* base = pool + static_cast<int64_t>(page) * (INT4 ? pe / 2 : pe);
             for (int64_t e = threadIdx.x * 8; e < pe; e += kAppendThreads * 8) {
                 const int t = static_cast<int>(e / row);
                 const int tok = page_start + t;
@@ -252,21 +307,7 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_kernel(AppendParams 
                 float v[8];
                 if (tok < old) Vec8<ST>::load(staging + static_cast<int64_t>(t) * row + c, v);
                 else Vec8<NT>::load(src_new + static_cast<int64_t>(tok - old) * row + c, v);
-                if (!INT4) {
-                    uint32_t w0 = 0, w1 = 0;
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        w0 |= (static_cast<uint32_t>(quant_code(v[i], sf, 127.0f)) & 0xFFu) << (8 * i);
-                        w1 |= (static_cast<uint32_t>(quant_code(v[4 + i], sf, 127.0f)) & 0xFFu) << (8 * i);
-                    }
-                    *reinterpret_cast<uint2*>(pool + static_cast<int64_t>(page) * pe + e) = make_uint2(w0, w1);
-                } else {
-                    uint32_t w = 0;
-#pragma unroll
-                    for (int i = 0; i < 8; ++i)
-                        w |= (static_cast<uint32_t>(quant_code(v[i], sf, 7.0f)) & 0xFu) << (4 * i);
-                    *reinterpret_cast<uint32_t*>(pool + static_cast<int64_t>(page) * (pe / 2) + e / 2) = w;
-                }
+                store_codes<INT4>(base, e, v, sf);
             }
         }
     }
@@ -303,6 +344,8 @@ struct GatherParams {
     const int32_t* cu_seqlens;
     int32_t P;
     int32_t row;
+    int32_t D;
+    int32_t scale_th;  // scales [N, P, Hkv] instead of [N]
     int64_t num_pages;
     int32_t include_staging;
     void* out_k;
@@ -329,10 +372,16 @@ __global__ void __launch_bounds__(kGatherThreads) gather_dequant_kernel(GatherPa
             if (threadIdx.x == 0) flag(p.status, MG_DEV_BAD_PAGE_ID);
             page = 0;
         }
-        const float sf = (kv ? p.v_scales : p.k_scales)[page];
+        const float* scales = kv ? p.v_scales : p.k_scales;
+        const float sf_page = p.scale_th ? 0.0f : scales[page];
         const uint8_t* pool = static_cast<const uint8_t*>(kv ? p.v_pool : p.k_pool);
         for (int64_t e = threadIdx.x * 8; e < pe; e += kGatherThreads * 8) {
             float v[8];
+            float sf = sf_page;
+            if (p.scale_th) {  // the scale of this (token, head) D-vector
+                const int t = static_cast<int>(e / row);
+                sf = scales[(static_cast<int64_t>(page) * P + t) * (row / p.D) + (e - static_cast<int64_t>(t) * row) / p.D];
+            }
             if (!INT4) {
                 const uint2 w = *reinterpret_cast<const uint2*>(pool + static_cast<int64_t>(page) * pe + e);
 #pragma unroll
@@ -372,6 +421,10 @@ mg_status check_layout(const mg_cache_layout* L) {
                "INT4 pools need head_dim % 32 == 0 (16-byte rows), got %d", L->head_dim);
     MG_REQUIRE(L->max_blocks >= 1, "max_blocks must be positive");
     MG_REQUIRE(L->num_pages >= 1 && L->num_pages < (1ll << 31), "num_pages out of range");
+    MG_REQUIRE(L->scale_layout == MG_SCALE_PAGE || L->scale_layout == MG_SCALE_TOKEN_HEAD,
+               "scale_layout must be MG_SCALE_PAGE or MG_SCALE_TOKEN_HEAD");
+    MG_REQUIRE(L->scale_layout == MG_SCALE_PAGE || (L->head_dim <= 256 && (L->head_dim & (L->head_dim - 1)) == 0),
+               "MG_SCALE_TOKEN_HEAD needs head_dim a power of two <= 256, got %d", L->head_dim);
     return MG_OK;
 }
 
@@ -462,6 +515,8 @@ extern "C" mg_status mg_kv_append(const mg_cache_layout* L, const mg_layer_ptrs*
     p.n_new = n_new;
     p.P = L->page_size;
     p.row = L->num_kv_heads * L->head_dim;
+    p.D = L->head_dim;
+    p.scale_th = L->scale_layout == MG_SCALE_TOKEN_HEAD;
     p.num_pages = L->num_pages;
     p.status = dev_status;
     const int touch = (max_new + L->page_size - 1) / L->page_size + 1;
@@ -503,6 +558,8 @@ extern "C" mg_status mg_gather_dequant(const mg_cache_layout* L, const mg_layer_
     p.cu_seqlens = cu_seqlens;
     p.P = L->page_size;
     p.row = L->num_kv_heads * L->head_dim;
+    p.D = L->head_dim;
+    p.scale_th = L->scale_layout == MG_SCALE_TOKEN_HEAD;
     p.num_pages = L->num_pages;
     p.include_staging = include_staging;
     p.out_k = out_k;

@@ -147,6 +147,42 @@ def dequantize_int4(packed: np.ndarray, offset: int, num_tokens: int, scale: flo
     return out
 
 
+def quantize_token_head(x, kv_dtype: str = "int8"):
+    """One fresh absmax scale per (token, head) D-vector: the reference's
+    ``quantize_new_scale`` / ``quantize_int4_new_scale`` (csrc/quantize.cu:65-120,
+    csrc/quantize_int4.cu:67-125) applied to each ``[1, 1, D]`` slice of
+    ``x[T, H, D]``.  The reference cache has only per-page scales
+    (metagross/cache.py:39,69-70); this is the per-token-per-head layout of its
+    CPU reference config, with the kernels' rounding.
+    Returns ``(codes [T, H, D] int8 or [T, H, D/2] uint8, scales float64 [T, H])``."""
+    x = _f32(x)
+    T, H, D = x.shape
+    int8 = kv_dtype == "int8"
+    codes = np.zeros((T, H, D if int8 else D // 2), np.int8 if int8 else np.uint8)
+    scales = np.zeros((T, H), np.float64)
+    for t in range(T):
+        for h in range(H):
+            sl = x[t:t + 1, h:h + 1]
+            c, sc = quantize_int8(sl) if int8 else quantize_int4(sl)
+            codes[t, h] = c[0, 0]
+            scales[t, h] = sc
+    return codes, scales
+
+
+def dequantize_token_head(codes: np.ndarray, scales: np.ndarray, kv_dtype: str = "int8") -> np.ndarray:
+    """Inverse of ``quantize_token_head``: each [D] vector dequantized with its
+    own scale as csrc/dequantize.cu:9-26 / csrc/dequantize_int4.cu:9-37 do."""
+    T, H = codes.shape[:2]
+    D = codes.shape[2] if kv_dtype == "int8" else 2 * codes.shape[2]
+    out = np.empty((T, H, D), np.float32)
+    for t in range(T):
+        for h in range(H):
+            sl = codes[t:t + 1, h:h + 1]
+            out[t, h] = (dequantize_int8(sl, 0, 1, scales[t, h]) if kv_dtype == "int8"
+                         else dequantize_int4(sl, 0, 1, scales[t, h]))[0, 0]
+    return out
+
+
 def allocator_replay(num_pages: int, ops, free_list: np.ndarray | None = None):
     """Replay allocate (-1) / free (id) ops; returns (results, free_list, n_free)."""
     if free_list is None:
@@ -214,23 +250,26 @@ class PagedCacheModel:
     """Replay of the reference cache semantics for B sequences on one pool.
 
     kv_dtype "int8": pools int8 [N, P, Hkv, D]; "int4": uint8 [N, P, Hkv, D/2].
-    One fp32 scale per physical page for K and one for V
-    (metagross/cache.py:39,69-70).  Staged tokens are kept exactly
-    (metagross/cache.py:57-61) in ``staging_dtype``.
+    scale_granularity "page": one fp32 scale per physical page for K and one
+    for V (metagross/cache.py:39,69-70); "token_head": one per (page, token,
+    kv head), scales [N, P, Hkv] (``quantize_token_head``).  Staged tokens are
+    kept exactly (metagross/cache.py:57-61) in ``staging_dtype``.
     """
 
     def __init__(self, batch, num_pages, page_size, num_kv_heads, head_dim,
-                 kv_dtype="int8", staging_dtype=np.float32, max_blocks=None):
+                 kv_dtype="int8", staging_dtype=np.float32, max_blocks=None, scale_granularity="page"):
         self.B, self.N, self.P, self.H, self.D = batch, num_pages, page_size, num_kv_heads, head_dim
         self.kv_dtype = kv_dtype
+        self.scale_granularity = scale_granularity
         row = head_dim if kv_dtype == "int8" else head_dim // 2
         dt = np.int8 if kv_dtype == "int8" else np.uint8
         self.k_pool = np.zeros((num_pages, page_size, num_kv_heads, row), dt)
         self.v_pool = np.zeros_like(self.k_pool)
-        self.k_scales = np.zeros(num_pages, np.float32)
-        self.v_scales = np.zeros(num_pages, np.float32)
-        self.k_scales64 = np.zeros(num_pages, np.float64)
-        self.v_scales64 = np.zeros(num_pages, np.float64)
+        sshape = (num_pages,) + ((page_size, num_kv_heads) if scale_granularity == "token_head" else ())
+        self.k_scales = np.zeros(sshape, np.float32)
+        self.v_scales = np.zeros(sshape, np.float32)
+        self.k_scales64 = np.zeros(sshape, np.float64)
+        self.v_scales64 = np.zeros(sshape, np.float64)
         self.max_blocks = max_blocks if max_blocks is not None else num_pages
         self.block_tables = np.zeros((batch, self.max_blocks), np.int32)
         self.num_blocks = np.zeros(batch, np.int32)
@@ -280,7 +319,10 @@ class PagedCacheModel:
         self.num_blocks[b] = j + 1
         kp = np.stack(self.staging_k[b]).astype(np.float32)
         vp = np.stack(self.staging_v[b]).astype(np.float32)
-        if self.kv_dtype == "int8":
+        if self.scale_granularity == "token_head":
+            self.k_pool[m], sk = quantize_token_head(kp, self.kv_dtype)
+            self.v_pool[m], sv = quantize_token_head(vp, self.kv_dtype)
+        elif self.kv_dtype == "int8":
             self.k_pool[m], sk = quantize_int8(kp, np.zeros_like(self.k_pool[m]))
             self.v_pool[m], sv = quantize_int8(vp, np.zeros_like(self.v_pool[m]))
         else:
@@ -317,7 +359,9 @@ class PagedCacheModel:
         parts = []
         for j in range(int(self.num_blocks[b])):
             m = int(self.block_tables[b, j])
-            if self.kv_dtype == "int8":
+            if self.scale_granularity == "token_head":
+                parts.append(dequantize_token_head(pool[m], scales[m], self.kv_dtype))
+            elif self.kv_dtype == "int8":
                 parts.append(dequantize_int8(pool[m], 0, self.P, scales[m]))
             else:
                 parts.append(dequantize_int4(pool[m], 0, self.P, scales[m]))

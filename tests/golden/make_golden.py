@@ -3,7 +3,7 @@
 Run in a container where the reference is mounted (it is NOT needed at test
 time; the .npz files are committed):
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py /root/reference [all|page|token_head]
 
 Every fixture is produced by calling the reference's code, never by this
 repository's code:
@@ -163,8 +163,79 @@ def main(ref_root: str):
         att[f"scale{i}"] = np.array([sc])
     att["n"] = np.array([len(cfgs)])
     np.savez_compressed(os.path.join(OUT, "attention_helpers.npz"), **att)
+
     print("wrote fixtures to", OUT)
 
 
+def make_token_head(ref_root: str):
+    """Per-token-per-head INT8 scales on a GPT-2-small decode step: batch 4, 12
+    heads, head_dim 64, contexts U[1, 512], fp32 N(0, 1) K/V/q.  As in the
+    reference cache, the full 16-token pages of a context are quantized and the
+    partial last page stays exact; each (token, head) D-vector of a full page is
+    quantized by the reference's CPU path on its own.  The output is the
+    reference's exact attention math (_staging_contribution) over the
+    dequantized pages followed by the exact tail.  The test regenerates the
+    inputs from the seed (th_inputs is the recipe), so only digests of the
+    committed codes / scales, the first page of each sequence in full, the
+    rounding ties (t, h, d, CPU-path code, kernel code) and the outputs are
+    stored."""
+    import hashlib
+
+    sys.path.insert(0, ref_root)
+    from tests import reference as R
+    from metagross import attention as A
+
+    lens, ks, vs, q = th_inputs()
+    th = {"lens": lens.numpy(), "q": q.numpy()}
+    for b in range(len(lens)):
+        deqs = {}
+        n = int(lens[b]) // 16 * 16  # committed rows
+        for name, x in (("k", ks[b]), ("v", vs[b])):
+            xn = x.numpy()[:n]
+            codes = np.zeros(xn.shape, np.int8)
+            scales = np.zeros(xn.shape[:2], np.float32)
+            deq = np.zeros(xn.shape, np.float32)
+            ties = []
+            for t in range(xn.shape[0]):
+                for h in range(xn.shape[1]):
+                    c, sc = R.quantize_symmetric_int8(xn[t, h])
+                    # x / s landing exactly on k + 0.5: the CPU path rounds half to
+                    # even (np.round), the reference's CUDA kernels half away from
+                    # zero (roundf); the fixture keeps the kernels' code and lists
+                    # the position with both codes
+                    r = xn[t, h] / sc
+                    for d in np.nonzero(np.abs(r - np.trunc(r)) == 0.5)[0]:
+                        away = int(np.clip(np.trunc(r[d]) + np.sign(r[d]), -127, 127))
+                        ties.append((t, h, d, int(c[d]), away))
+                        c[d] = away
+                    codes[t, h], scales[t, h] = c, np.float32(sc)
+                    deq[t, h] = R.dequantize_symmetric_int8(c, sc)
+            th[f"{name}_ties{b}"] = np.array(ties, np.int32).reshape(-1, 5)
+            th[f"{name}_codes_sha{b}"] = np.frombuffer(hashlib.sha256(codes.tobytes()).digest(), np.uint8)
+            th[f"{name}_scales_sha{b}"] = np.frombuffer(hashlib.sha256(scales.tobytes()).digest(), np.uint8)
+            th[f"{name}_codes_page0_{b}"] = codes[:16]
+            th[f"{name}_scales_page0_{b}"] = scales[:16]
+            deqs[name] = torch.cat([torch.from_numpy(deq), x[n:]])
+        m, ssum, wv = A._staging_contribution(q[b], deqs["k"], deqs["v"], 1.0 / 8)
+        th[f"out{b}"] = (wv / ssum.unsqueeze(-1)).numpy()
+    np.savez_compressed(os.path.join(OUT, "token_head_int8.npz"), **th)
+    print("wrote token_head_int8.npz to", OUT)
+
+
+def th_inputs():
+    """Seeded inputs of the per-token-per-head fixture: (lens [4], K list, V list, q [4, 12, 64])."""
+    g = _gen(7300)
+    lens = torch.randint(1, 513, (4,), generator=g, dtype=torch.int32)
+    ks = [torch.randn(int(n), 12, 64, generator=g) for n in lens]
+    vs = [torch.randn(int(n), 12, 64, generator=g) for n in lens]
+    q = torch.randn(4, 12, 64, generator=g)
+    return lens, ks, vs, q
+
+
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    which = sys.argv[2] if len(sys.argv) > 2 else "all"
+    if which in ("all", "page"):
+        main(root)
+    if which in ("all", "token_head"):
+        make_token_head(root)

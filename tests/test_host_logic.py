@@ -195,3 +195,13 @@ def test_repeat_kv_heads_layout():
 def test_empty_staging_is_identity():
     m, s, wv = _staging_contribution(torch.randn(4, 64), torch.empty(0, 4, 64), torch.empty(0, 4, 64), 0.125)
     assert torch.isinf(m).all() and (m < 0).all() and (s == 0).all() and (wv == 0).all()
+
+
+def test_batched_cache_scale_granularity_arguments():
+    """Rejected before anything is allocated (the cache itself lives on a GPU)."""
+    from metagross_b200.batched import BatchedPagedKVCache
+
+    with pytest.raises(ValueError):
+        BatchedPagedKVCache(1, 1, 4, 64, device="cpu", scale_granularity="token")
+    with pytest.raises(ValueError):  # per-vector absmax is reduced over a power-of-two head_dim
+        BatchedPagedKVCache(1, 1, 4, 96, device="cpu", scale_granularity="token_head")

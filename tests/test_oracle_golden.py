@@ -157,3 +157,43 @@ def test_offset_write_leaves_other_tokens():
     O.quantize_int8(a * 2, page, 8, scale=0.05)
     np.testing.assert_array_equal(page[:8], before[:8])
     assert (page[8:] != 0).any()
+
+
+def _th_inputs():
+    """The seeded inputs of token_head_int8.npz (recipe in tests/golden/make_golden.py)."""
+    import sys
+
+    if GOLD not in sys.path:
+        sys.path.insert(0, GOLD)
+    import make_golden
+
+    return make_golden.th_inputs()
+
+
+def test_token_head_int8_matches_reference_cpu_path():
+    """Per-(token, head) INT8 scales on the GPT-2-small CPU-reference decode step
+    (batch 4, 12 heads, head_dim 64, contexts U[1, 512], full pages quantized,
+    the partial page exact): the oracle's codes and fp32 scales hash to the
+    fixture's (the reference's CPU path, with the CUDA kernels'
+    half-away-from-zero rounding at the listed ties), and its float64
+    dequantize-then-attend is within 1e-5 of the reference's fp32 torch math."""
+    import hashlib
+
+    z = _load("token_head_int8.npz")
+    lens, ks, vs, q = _th_inputs()
+    assert lens.numpy().tolist() == z["lens"].tolist()
+    for b in range(len(lens)):
+        n = int(lens[b]) // 16 * 16
+        deq = {}
+        for name, x in (("k", ks[b]), ("v", vs[b])):
+            codes, sc = O.quantize_token_head(x.numpy()[:n], "int8")
+            s32 = sc.astype(np.float32)
+            np.testing.assert_array_equal(codes[:16], z[f"{name}_codes_page0_{b}"])
+            np.testing.assert_array_equal(s32[:16], z[f"{name}_scales_page0_{b}"])
+            for t, h, d, _cpu_code, kernel_code in z[f"{name}_ties{b}"]:
+                assert codes[t, h, d] == kernel_code
+            assert hashlib.sha256(codes.tobytes()).digest() == z[f"{name}_codes_sha{b}"].tobytes()
+            assert hashlib.sha256(s32.tobytes()).digest() == z[f"{name}_scales_sha{b}"].tobytes()
+            deq[name] = np.concatenate([O.dequantize_token_head(codes, sc, "int8"), x.numpy()[n:]])
+        out = O.attention(q[b].numpy(), deq["k"], deq["v"], 1.0 / 8)
+        np.testing.assert_allclose(out, z[f"out{b}"], atol=1e-5, rtol=0)

@@ -117,3 +117,36 @@ def test_paged_attention_committed_matches_reference(hq, hkv, pages, P):
     np.testing.assert_allclose(wo.cpu().numpy(), wr.cpu().numpy(), rtol=1e-4, atol=1e-4)
     # the normalised outputs, which are what a caller uses
     np.testing.assert_allclose((wo / lo[:, None]).cpu().numpy(), (wr / lr[:, None]).cpu().numpy(), atol=2e-5)
+
+
+@pytest.mark.parametrize("kv", ["int8", "int4"])
+def test_token_head_commit_matches_reference_per_vector(kv):
+    """Pages committed with one scale per (token, head): every D-vector's codes /
+    nibbles and fp32 scale equal the reference's own quantize op run on that
+    [1, 1, D] slice (NaN, zero and outlier elements included)."""
+    from metagross_b200.batched import BatchedPagedKVCache
+
+    ref = _ref()
+    H, D, P = 4, 64, 16
+    x = _inputs(41, 2 * P, H, D, special=True)
+    x[3, 1] = 0.0  # an all-zero vector: scale 1e-8
+    y = _inputs(42, 2 * P, H, D) * 0.5
+    cache = BatchedPagedKVCache(1, 1, H, D, page_size=P, num_pages=4, max_blocks=4, kv_dtype=kv,
+                                staging_dtype=torch.float32, scale_granularity="token_head")
+    cache.begin_step(torch.tensor([2 * P], dtype=torch.int32))
+    cache.append(0, x[None].cuda(), y[None].cuda())
+    cache.check()
+    bt = cache.block_tables[0, :2].cpu().tolist()
+    for src, pool, scales in ((x, cache.k_pool[0], cache.k_scales[0]), (y, cache.v_pool[0], cache.v_scales[0])):
+        for j, page in enumerate(bt):
+            for t in range(P):
+                for h in range(H):
+                    sl = src[j * P + t:j * P + t + 1, h:h + 1].contiguous().cuda()
+                    if kv == "int8":
+                        buf = torch.zeros(1, 1, D, dtype=torch.int8, device="cuda")
+                        s = ref.quantize_new_scale(sl, buf, 0)
+                    else:
+                        buf = torch.zeros(1, 1, D // 2, dtype=torch.uint8, device="cuda")
+                        s = ref.quantize_int4_new_scale(sl, buf, 0)
+                    assert np.float32(s) == scales[page, t, h].item(), (page, t, h)
+                    assert torch.equal(buf[0, 0], pool[page, t, h]), (page, t, h)

@@ -21,7 +21,7 @@ MG_F32, MG_F16 = 0, 1
 class Layout(ctypes.Structure):
     _fields_ = [("kv_dtype", ctypes.c_int32), ("staging_dtype", ctypes.c_int32), ("page_size", ctypes.c_int32),
                 ("num_kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("max_blocks", ctypes.c_int32),
-                ("num_pages", ctypes.c_int64)]
+                ("num_pages", ctypes.c_int64), ("scale_layout", ctypes.c_int32), ("reserved", ctypes.c_int32)]
 
 
 class LayerPtrs(ctypes.Structure):
