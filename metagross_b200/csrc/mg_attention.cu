@@ -72,7 +72,7 @@ mg_status make_decode_plan(int kv4, int hd, int P, int Hkv, int Hq, int q_f16, i
     const int64_t scratch_bytes =
         pl.wph > 1 ? align_up(static_cast<int64_t>(pl.nconsumers) * pl.nt * ncols * 4 * (hd + 2) * 4, 128) : 0;
     int64_t slot = 0;
-    if (staging_esize > 0) {
+    if (staging_esize == 4) {  // fp32 tails go through shared memory (fp16 tails: straight to registers)
         const int64_t row = static_cast<int64_t>(hd) * staging_esize;  // one staged row of one head
         slot = 2 * row > 2048 ? 2 * row : 2048;
         // shrink to one row pair per slot when the batch needs the room
@@ -234,6 +234,8 @@ mg_status prepare_batched(const mg_cache_layout* L, const mg_layer_ptrs* lp, con
     MG_REQUIRE(out_dtype == MG_F32 || out_dtype == MG_F16, "out_dtype must be MG_F32 or MG_F16");
     MG_REQUIRE(scale > 0.0f && scale < 1.0f / 0.0f, "attention scale must be positive and finite");
     MG_REQUIRE(aligned16(lp->k_pool) && aligned16(lp->v_pool), "pools must be 16-byte aligned");
+    MG_REQUIRE(!(lp->staging_k && lp->staging_v) || (aligned16(lp->staging_k) && aligned16(lp->staging_v)),
+               "staging buffers must be 16-byte aligned");
     MG_REQUIRE(aligned16(out), "out must be 16-byte aligned");
     const bool staged = lp->staging_k && lp->staging_v;
     DecodePlan pl;

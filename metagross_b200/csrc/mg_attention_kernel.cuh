@@ -6,14 +6,17 @@
 
 namespace mg {
 
-// One 16-token tile of one kv head, already in registers: S^T = K Q^T on the
-// tensor cores, online softmax update, O^T += V^T P^T.  sscale: softmax scale
-// times log2(e).
-template <bool KV4, int HD, int NT, bool SPLIT, bool P16>
-__device__ __forceinline__ void attend_tile(HeadState<NT, HD / 16>& S, const TileRegs<KV4, HD>& T, float sscale) {
+// The math of one 16-token tile of one kv head: S^T = K Q^T on the tensor
+// cores, online softmax update, O^T += V^T P^T.  The fp16 fragments come from
+// kf(kk, a): K rows g, g+8 of k-step kk (a[0], a[2] row g; a[1], a[3] row g+8),
+// and vf(r0a, r1a, r0b, r1b): V^T for tokens (2c, 2c+1) and (2c+8, 2c+9).
+// ks0 / ks1: K scales of rows g / g+8 times the softmax scale (log2 domain),
+// vs0 / vs1 their V scales; live0 / live1: the rows exist.
+template <bool KV4, int HD, int NT, bool SPLIT, typename KF, typename VF>
+__device__ __forceinline__ void attend_core(HeadState<NT, HD / 16>& S, KF&& kf, VF&& vf, float ks0, float ks1,
+                                            float vs0, float vs1, bool live0, bool live1) {
     using C = Cfg<KV4, HD, NT>;
     constexpr int NCOLS = SPLIT ? 1 : 2;
-    const bool live0 = (T.live & 1u) != 0, live1 = (T.live & 2u) != 0;
 
     // ---- scores: K rows g, g+8 against the q columns ------------------------------
     float sc[NT][4], sc2[NT][4];  // two accumulation chains (even / odd k-steps)
@@ -24,18 +27,13 @@ __device__ __forceinline__ void attend_tile(HeadState<NT, HD / 16>& S, const Til
 #pragma unroll
     for (int kk = 0; kk < C::KSTEPS; ++kk) {
         uint32_t a[4];
-        k_frag_row<KV4>(T.k[0], kk, a[0], a[2]);
-        k_frag_row<KV4>(T.k[1], kk, a[1], a[3]);
+        kf(kk, a);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
             if (kk & 1) mma_16816(sc2[nt], a, S.qf[nt][kk][0], S.qf[nt][kk][1]);
             else mma_16816(sc[nt], a, S.qf[nt][kk][0], S.qf[nt][kk][1]);
         }
     }
-    // page size 16 (page scales): one page per tile, its scales live in slot 0 only
-    const float ks0 = T.ks[0] * sscale, ks1 = T.ks[P16 ? 0 : 1] * sscale;
-    const float vs0 = T.vs[0], vs1 = T.vs[P16 ? 0 : 1];
-
     // ---- online softmax (log2 domain, lazy rescale) ---------------------------------
     float s[NT][NCOLS][2];
 #pragma unroll
@@ -118,14 +116,98 @@ __device__ __forceinline__ void attend_tile(HeadState<NT, HD / 16>& S, const Til
 
     // ---- V: tokens 2c, 2c+1, 2c+8, 2c+9 -------------------------------------------
     uint32_t r0a[C::MTILES], r1a[C::MTILES], r0b[C::MTILES], r1b[C::MTILES];
-    v_pairs<KV4, HD>(T.v[0], T.v[1], r0a, r1a);
-    v_pairs<KV4, HD>(T.v[2], T.v[3], r0b, r1b);
+    vf(r0a, r1a, r0b, r1b);
 #pragma unroll
     for (int mt = 0; mt < C::MTILES; ++mt) {
         const uint32_t a[4] = {r0a[mt], r1a[mt], r0b[mt], r1b[mt]};
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) mma_16816(S.acc[mt][nt], a, pb[nt][0], pb[nt][1]);
     }
+}
+
+// One 16-token tile of quantized pages, already in registers (TileRegs).
+// sscale: softmax scale times log2(e).
+template <bool KV4, int HD, int NT, bool SPLIT, bool P16>
+__device__ __forceinline__ void attend_tile(HeadState<NT, HD / 16>& S, const TileRegs<KV4, HD>& T, float sscale) {
+    // page size 16 (page scales): one page per tile, its scales live in slot 0 only
+    const float ks0 = T.ks[0] * sscale, ks1 = T.ks[P16 ? 0 : 1] * sscale;
+    const float vs0 = T.vs[0], vs1 = T.vs[P16 ? 0 : 1];
+    attend_core<KV4, HD, NT, SPLIT>(
+        S,
+        [&](int kk, uint32_t (&a)[4]) {
+            k_frag_row<KV4>(T.k[0], kk, a[0], a[2]);
+            k_frag_row<KV4>(T.k[1], kk, a[1], a[3]);
+        },
+        [&](uint32_t (&r0a)[HD / 16], uint32_t (&r1a)[HD / 16], uint32_t (&r0b)[HD / 16], uint32_t (&r1b)[HD / 16]) {
+            v_pairs<KV4, HD>(T.v[0], T.v[1], r0a, r1a);
+            v_pairs<KV4, HD>(T.v[2], T.v[3], r0b, r1b);
+        },
+        ks0, ks1, vs0, vs1, (T.live & 1u) != 0, (T.live & 2u) != 0);
+}
+
+// One 16-row tile of the exact fp16 staged tail of kv head h of sequence b:
+// staged rows r0 .. r0 + n - 1 (n <= 16), straight from global memory (the
+// append kernel wrote them just before; an L1 prefetch went out when the item
+// was issued).  The fp16 rows are the tensor-core operands as they are: K in
+// the q columns' dimension order (k_slot_d), V^T paired by token, no scales.
+template <bool KV4, int HD, int NT, bool SPLIT>
+__device__ __forceinline__ void attend_tail_tile(HeadState<NT, HD / 16>& S, const DecodeParams& p, int b, int h,
+                                                 int r0, int n, int g, int c, float sscale) {
+    constexpr int KW = HD / 8;   // 32-bit words per lane of a K row: HD / 4 halves
+    constexpr int VW = HD / 16;  // of a V row: HD / 8 halves
+    const int64_t rs = static_cast<int64_t>(p.Hkv) * HD;  // halves per staged token row
+    const __half* base = static_cast<const __half*>(p.staging_k) + ((static_cast<int64_t>(b) * p.P + r0) * p.Hkv + h) * HD;
+    const __half* vbase = static_cast<const __half*>(p.staging_v) + (base - static_cast<const __half*>(p.staging_k));
+    uint32_t kw[2][KW], vw[4][VW];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const int row = g + 8 * r;
+        const uint4* src = reinterpret_cast<const uint4*>(base + row * rs + (HD / 4) * c);
+#pragma unroll
+        for (int i = 0; i < KW / 4; ++i) {
+            const uint4 u = row < n ? src[i] : make_uint4(0u, 0u, 0u, 0u);
+            kw[r][4 * i] = u.x;
+            kw[r][4 * i + 1] = u.y;
+            kw[r][4 * i + 2] = u.z;
+            kw[r][4 * i + 3] = u.w;
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const int row = 2 * c + (r & 1) + (r >> 1) * 8;
+        const uint4* src = reinterpret_cast<const uint4*>(vbase + row * rs + (HD / 8) * g);
+#pragma unroll
+        for (int i = 0; i < VW / 4; ++i) {
+            const uint4 u = row < n ? src[i] : make_uint4(0u, 0u, 0u, 0u);
+            vw[r][4 * i] = u.x;
+            vw[r][4 * i + 1] = u.y;
+            vw[r][4 * i + 2] = u.z;
+            vw[r][4 * i + 3] = u.w;
+        }
+    }
+    attend_core<KV4, HD, NT, SPLIT>(
+        S,
+        [&](int kk, uint32_t (&a)[4]) {
+            // k_slot_d: a[0] = dims (d0, d0 + 2 or 4), a[2] = (d0 + 1, d0 + 3 or 5), d0 even
+            const int i0 = KV4 ? 4 * (kk >> 1) + (kk & 1) : 2 * kk;
+            const int i1 = KV4 ? i0 + 2 : i0 + 1;
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                a[r] = __byte_perm(kw[r][i0], kw[r][i1], 0x5410);
+                a[r + 2] = __byte_perm(kw[r][i0], kw[r][i1], 0x7632);
+            }
+        },
+        [&](uint32_t (&r0a)[HD / 16], uint32_t (&r1a)[HD / 16], uint32_t (&r0b)[HD / 16], uint32_t (&r1b)[HD / 16]) {
+            // m-tile mt: dims VE*g + 2mt (r0) and + 1 (r1), tokens paired
+#pragma unroll
+            for (int mt = 0; mt < HD / 16; ++mt) {
+                r0a[mt] = __byte_perm(vw[0][mt], vw[1][mt], 0x5410);
+                r1a[mt] = __byte_perm(vw[0][mt], vw[1][mt], 0x7632);
+                r0b[mt] = __byte_perm(vw[2][mt], vw[3][mt], 0x5410);
+                r1b[mt] = __byte_perm(vw[2][mt], vw[3][mt], 0x7632);
+            }
+        },
+        sscale, sscale, 1.0f, 1.0f, g < n, g + 8 < n);
 }
 
 template <bool KV4, int HD, int NT, bool SPLIT>
@@ -264,10 +346,12 @@ __device__ __forceinline__ void attend_tail_chunk(HeadState<NT, HD / 16>& S, con
 
 // A piece of one sequence run by this CTA (one record of the decode plan),
 // and this warp's work items in it: its tiles (segment tiles wsub,
-// wsub + wph, ..., times the warp's heads) and its chunks of the staged tail
-// (rows wsub, wsub + wph, ..., up to tt rows per chunk, times the warp's
-// heads).  The tail chunks come first: their CUDA-core math then overlaps the
-// ramp of the page stream instead of trailing it.
+// wsub + wph, ..., times the warp's heads) and its chunks of the staged tail,
+// times the warp's heads.  An fp16 tail goes in 16-row tiles on the tensor
+// cores: tail tile j to warp (j + ntiles) % wph, i.e. first to the warps that
+// hold one page tile fewer.  An fp32 tail goes on the CUDA cores in chunks of
+// up to tt rows (rows wsub, wsub + wph, ...).  The tail items come first: they
+// then overlap the ramp of the page stream instead of trailing it.
 struct Segment {
     int b;
     int lo;      // first committed page of the segment (sequence-relative)
@@ -279,13 +363,14 @@ struct Segment {
     bool complete;
     int nh;      // the warp's heads (1, or 2 with two heads per warp)
     int ntile;   // the warp's tile items
-    int ntt;     // the warp's tail rows (per head)
-    int nchunk;  // its tail chunks (per head)
+    int ntt;     // the warp's tail rows (per head; fp32 tails)
+    int tj0;     // its first 16-row tail tile (fp16 tails)
+    int nchunk;  // its tail chunks or tail tiles (per head)
     int ntail;   // its tail items, nchunk * nh: items [0, ntail), its tiles after them
     int nitems;  // ntail + ntile
 };
 
-__device__ __forceinline__ Segment make_segment(const int4* rec, int P, int wsub, int wph, int nh, int tt) {
+__device__ __forceinline__ Segment make_segment(const int4* rec, int P, int wsub, int wph, int nh, int tt, bool tc) {
     Segment s;
     const int4 r0 = rec[0], r1 = rec[1];
     s.b = r0.x;
@@ -300,8 +385,17 @@ __device__ __forceinline__ Segment make_segment(const int4* rec, int P, int wsub
     const int ntiles = P == 16 ? s.npg : (s.npg * P + 15) >> 4;
     const int nloc = wsub < ntiles ? (ntiles - 1 - wsub) / wph + 1 : 0;
     s.ntile = nloc * nh;
-    s.ntt = wsub < s.tail ? (s.tail - 1 - wsub) / wph + 1 : 0;
-    s.nchunk = (s.ntt + tt - 1) / tt;
+    if (tc) {
+        const int nT = (s.tail + 15) >> 4;
+        s.tj0 = wsub - ntiles % wph;
+        if (s.tj0 < 0) s.tj0 += wph;
+        s.ntt = 0;
+        s.nchunk = s.tj0 < nT ? (nT - 1 - s.tj0) / wph + 1 : 0;
+    } else {
+        s.tj0 = 0;
+        s.ntt = wsub < s.tail ? (s.tail - 1 - wsub) / wph + 1 : 0;
+        s.nchunk = (s.ntt + tt - 1) / tt;
+    }
     s.ntail = s.nchunk * nh;
     s.nitems = s.ntail + s.ntile;
     return s;
@@ -618,14 +712,15 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
     const int h1 = (HPW == 2 && hbase + NCW < Hkv) ? hbase + NCW : -1;  // second head, if any
     const int nh = h1 >= 0 ? 2 : 1;
     const int hb = HD * (p.st_f16 ? 2 : 4);      // bytes of one staged row of one head
-    const int tt = p.tail_slot > 0 ? p.tail_slot / (2 * hb) : 1;  // staged rows per tail chunk
+    const int tt = p.tail_slot > 0 ? p.tail_slot / (2 * hb) : 1;  // staged rows per tail chunk (fp32)
+    const bool tc = p.st_f16 != 0;  // fp16 tail: 16-row tiles on the tensor cores
     HeadState<NT, HD / 16> st[HPW];
     TileRegs<KV4, HD> tb[R];
     MetaCache mc;
 
     // ---- issuing walk: runs R - 1 items ahead of the math, across segments -------
     int sidx = 0;
-    Segment si = make_segment(rec(0), p.P, wsub, WPH, nh, tt);
+    Segment si = make_segment(rec(0), p.P, wsub, WPH, nh, tt, tc);
     int ji = 0;
     bool idone = false;
     mc.base = -(1 << 30);
@@ -639,7 +734,7 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
             if (++sidx >= nseg) {
                 idone = true;
             } else {
-                si = make_segment(rec(sidx), p.P, wsub, WPH, nh, tt);
+                si = make_segment(rec(sidx), p.P, wsub, WPH, nh, tt, tc);
                 ji = 0;
                 mc.base = -(1 << 30);
                 mc.spids = nullptr;
@@ -656,6 +751,19 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
                 with_slot<R>(iphase, [&](auto k) {
                     load_tile<KV4, HD, P16>(tb[decltype(k)::value], mc, p, si, jt, nloc, h, wsub, WPH, g, c, lane);
                 });
+            } else if (tc) {
+                // fp16 tail tile: warm L1 with its rows (lane l: K row l or V row l - 16)
+                const int q = ji;
+                const int hh = q / si.nchunk, chunk = q - hh * si.nchunk;
+                const int r0 = 16 * (si.tj0 + WPH * chunk);
+                const int row = r0 + (lane & 15);
+                if (row < si.tail) {
+                    const __half* st16 = static_cast<const __half*>(lane < 16 ? p.staging_k : p.staging_v);
+                    const __half* rp =
+                        st16 + ((static_cast<int64_t>(si.b) * p.P + row) * p.Hkv + (hh ? h1 : hbase)) * HD;
+#pragma unroll
+                    for (int l = 0; l < HD * 2; l += 128) prefetch_l1(reinterpret_cast<const char*>(rp) + l);
+                }
             } else {
                 const int q = ji;
                 const int hh = q / si.nchunk, chunk = q - hh * si.nchunk;
@@ -686,6 +794,14 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
                 if (second) attend_tile<KV4, HD, NT, SPLIT, P16>(st[HPW - 1], cur, p.sm_scale_log2);
                 else attend_tile<KV4, HD, NT, SPLIT, P16>(st[0], cur, p.sm_scale_log2);
             }
+        } else if (tc) {
+            const int q = j;
+            const int hh = q / sc.nchunk, chunk = q - hh * sc.nchunk;
+            const int r0 = 16 * (sc.tj0 + WPH * chunk);
+            const int n = min(16, sc.tail - r0);
+            if (HPW == 2 && hh)
+                attend_tail_tile<KV4, HD, NT, SPLIT>(st[HPW - 1], p, sc.b, h1, r0, n, g, c, p.sm_scale_log2);
+            else attend_tail_tile<KV4, HD, NT, SPLIT>(st[0], p, sc.b, hbase, r0, n, g, c, p.sm_scale_log2);
         } else {
             const int q = j;
             const int hh = q / sc.nchunk, chunk = q - hh * sc.nchunk;
@@ -709,7 +825,7 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
 
     // ---- consuming walk: every segment of the CTA, in order -----------------------
     for (int cidx = 0; cidx < nseg; ++cidx) {
-        const Segment sc = make_segment(rec(cidx), p.P, wsub, WPH, nh, tt);
+        const Segment sc = make_segment(rec(cidx), p.P, wsub, WPH, nh, tt, tc);
         const int b = sc.b;
 #pragma unroll
         for (int hh = 0; hh < HPW; ++hh) {
