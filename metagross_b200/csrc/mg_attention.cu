@@ -34,19 +34,16 @@ mg_status make_decode_plan(int kv4, int hd, int P, int Hkv, int Hq, int q_f16, i
     if (pl.nt > 2) return set_error(MG_ERR_UNSUPPORTED, "GQA group %d too large (fp32 q: <= 8, fp16 q: <= 16)", G);
     // warps: one kv head each, several warps per head when there are few kv
     // heads, two heads per warp (head_dim 64, one n-tile) beyond that.  Head
-    // dim 64 with one n-tile picks 12 or 16 warps by the bytes each SM keeps
-    // in flight (warps with a head x (ring - 1) tiles; 12 on a tie); the
+    // dim 64 with one n-tile runs 12 warps at 168 registers unless 16 warps of
+    // 128 registers put a third more warps on the kv heads (12 warps measured
+    // 23.5 us per launch against 25.6 / 28.5 with 16 warps and a ring of 2 / 4
+    // on the TinyLlama shape, 27.5 against 30.1 on the GPT-2 shape); the
     // register-heavy shapes (head_dim 128, two n-tiles) run 8 wide warps when
     // there are at most 8 kv heads.
     const bool light = hd == 64 && pl.nt == 1;
-    const int tile_bytes = 16 * (kv4 ? hd / 2 : hd);
     if (light && Hkv <= kWarps) {
-        auto in_flight = [&](int nw) -> int64_t {
-            if (Hkv > nw) return -1;
-            const int used = Hkv * (nw / Hkv);
-            return static_cast<int64_t>(used) * (decode_ring(kv4 != 0, hd, pl.nt, 1, nw) - 1) * tile_bytes;
-        };
-        pl.nwarps = in_flight(kWarpsDeep) >= in_flight(kWarps) ? kWarpsDeep : kWarps;
+        auto used = [&](int nw) -> int { return Hkv <= nw ? Hkv * (nw / Hkv) : 0; };
+        pl.nwarps = 4 * used(kWarpsDeep) >= 3 * used(kWarps) ? kWarpsDeep : kWarps;
     } else {
         pl.nwarps = (!light && Hkv <= kWarpsWide) ? kWarpsWide : kWarps;
     }

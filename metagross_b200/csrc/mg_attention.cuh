@@ -56,20 +56,18 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 2^8 in fp16
 constexpr int kMetaLanes = 32;             // page ids cached per warp (one per lane)
 constexpr int kPrefetchTiles = 8;          // L2 prefetch distance of a warp's tile stream (tiles)
 
-// Work items (tiles or staged-tail chunks) in flight per warp (R - 1 of them
+// Work items (tiles or staged-tail items) in flight per warp (R - 1 of them
 // are loading while one is computed), by register budget and measurement.  The
 // L2 prefetch kPrefetchTiles ahead covers the DRAM latency, so the register
-// ring mostly covers L2 hits; INT8 at 12 warps runs a ring of two (a deeper one
-// makes every warp issue more loads before its first tile and lengthens the
-// launch's prologue by ~2 us), INT4 tiles are half the registers and keep five:
-//   head_dim 64, one n-tile, 12 warps (168 registers):      5 INT4, 2 INT8
+// ring only covers L2 hits; a deeper ring makes every warp issue more loads
+// before its first tile, ~1 us of launch prologue per extra item:
+//   head_dim 64, one n-tile, 12 warps (168 registers):      2
 //   head_dim 64, one n-tile, 16 warps (128 registers):      4 INT4, 2 INT8,
 //                                                            2 with two kv heads per warp
 //   head_dim 128 or two n-tiles, 8 warps (255 registers):   2
 //   head_dim 128 or two n-tiles, 16 warps:                   1
 __host__ __device__ constexpr int decode_ring(bool kv4, int hd, int nt, int hpw, int nwarps) {
-    return (hd == 64 && nt == 1) ? (hpw == 2 ? 2 : nwarps == 12 ? (kv4 ? 5 : 2) : (kv4 ? 4 : 2))
-                                 : (nwarps == 8 ? 2 : 1);
+    return (hd == 64 && nt == 1) ? (hpw == 2 || nwarps == 12 ? 2 : (kv4 ? 4 : 2)) : (nwarps == 8 ? 2 : 1);
 }
 
 // Decode plan buffer (int32 words), written once per step by the plan
