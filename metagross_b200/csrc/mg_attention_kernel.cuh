@@ -478,14 +478,19 @@ __device__ __forceinline__ void load_tile(TileRegs<KV4, HD>& T, MetaCache& mc, c
         }
         // L2 prefetch of the warp's tile kPrefetchTiles ahead: lane l brings K row l
         // (l < 16) or V row l - 16 of this head, lanes 0 and 16 also the page's K / V
-        // scale, so the register ring reads from L2
-        const int ja = jt + kPrefetchTiles;
-        if (ja < nloc && ja < mc.base + kMetaLanes) {
-            const int32_t pa = __shfl_sync(0xffffffffu, mc.pid, ja - mc.base);
-            const uint8_t* pool = lane < 16 ? p.k_pool : p.v_pool;
-            prefetch_l2(pool + static_cast<int64_t>(pa) * p.page_bytes + (lane & 15) * rs + h * C::ROWB);
-            if ((lane & 15) == 0) prefetch_l2((lane < 16 ? p.k_scales : p.v_scales) + pa);
-        }
+        // scale, so the register ring reads from L2.  The segment's first tile also
+        // sends the tiles between it and that distance.
+        auto prefetch_tile = [&](int ja) {
+            if (ja < nloc && ja < mc.base + kMetaLanes) {
+                const int32_t pa = __shfl_sync(0xffffffffu, mc.pid, ja - mc.base);
+                const uint8_t* pool = lane < 16 ? p.k_pool : p.v_pool;
+                prefetch_l2(pool + static_cast<int64_t>(pa) * p.page_bytes + (lane & 15) * rs + h * C::ROWB);
+                if ((lane & 15) == 0) prefetch_l2((lane < 16 ? p.k_scales : p.v_scales) + pa);
+            }
+        };
+        if (jt == 0)
+            for (int d = 1; d < kPrefetchTiles; ++d) prefetch_tile(d);
+        prefetch_tile(jt + kPrefetchTiles);
     } else {
         const int P = p.P;
         const int x0 = 16 * (wsub + jt * wph);  // first token of the tile (segment-relative)
