@@ -51,16 +51,16 @@ __device__ __forceinline__ void attend_core(HeadState<NT, HD / 16>& S, KF&& kf, 
             }
         }
     }
+    // The column max is reduced over the lanes (rows) only when some lane's
+    // score passes the reference max by the threshold; m_true stays a per-lane
+    // running max, reduced when the segment is finalized.
     bool need = false;
     float mx[NT][NCOLS];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int col = 0; col < NCOLS; ++col) {
-            float m = fmaxf(s[nt][col][0], s[nt][col][1]);
-            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
-            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
-            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+            const float m = fmaxf(s[nt][col][0], s[nt][col][1]);
             mx[nt][col] = m;
             S.m_true[nt][col] = fmaxf(S.m_true[nt][col], m);
             need |= m > S.m_used[nt][col] + kRescaleThreshold;
@@ -70,7 +70,11 @@ __device__ __forceinline__ void attend_core(HeadState<NT, HD / 16>& S, KF&& kf, 
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
             for (int col = 0; col < NCOLS; ++col) {
-                const float m_new = fmaxf(S.m_used[nt][col], mx[nt][col]);
+                float m = mx[nt][col];
+                m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+                m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
+                m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+                const float m_new = fmaxf(S.m_used[nt][col], m);
                 const float alpha = ex2(S.m_used[nt][col] - m_new);
                 S.m_used[nt][col] = m_new;
                 S.lpart[nt][col] *= alpha;
@@ -477,19 +481,22 @@ __device__ __forceinline__ void load_tile(TileRegs<KV4, HD>& T, MetaCache& mc, c
             ldg_words<C::VCHB>(vb + row * rs + g * C::VCHB, T.v[r]);
         }
         // L2 prefetch of the warp's tile kPrefetchTiles ahead: lane l brings K row l
-        // (l < 16) or V row l - 16 of this head, lanes 0 and 16 also the page's K / V
-        // scale, so the register ring reads from L2.  The segment's first tile also
-        // sends the tiles between it and that distance.
+        // (l < 16) or V row l - 16, lanes 0 and 16 also the page's K / V scale, so
+        // the register ring reads from L2.  Rows of neighbouring heads share
+        // 128-byte lines: when the page rows are line-aligned, only a warp whose
+        // head starts a line sends it.  The segment's first tiles also send the
+        // tiles before that distance, two per tile (tiles 2jt + 1 and 2jt + 2).
+        const bool pf_lead = (rs % 128 != 0) || ((h * C::ROWB) % 128 == 0);
         auto prefetch_tile = [&](int ja) {
-            if (ja < nloc && ja < mc.base + kMetaLanes) {
+            if (pf_lead && ja < nloc && ja < mc.base + kMetaLanes) {
                 const int32_t pa = __shfl_sync(0xffffffffu, mc.pid, ja - mc.base);
                 const uint8_t* pool = lane < 16 ? p.k_pool : p.v_pool;
                 prefetch_l2(pool + static_cast<int64_t>(pa) * p.page_bytes + (lane & 15) * rs + h * C::ROWB);
                 if ((lane & 15) == 0) prefetch_l2((lane < 16 ? p.k_scales : p.v_scales) + pa);
             }
         };
-        if (jt == 0)
-            for (int d = 1; d < kPrefetchTiles; ++d) prefetch_tile(d);
+        if (2 * jt + 1 < kPrefetchTiles) prefetch_tile(2 * jt + 1);
+        if (2 * jt + 2 < kPrefetchTiles) prefetch_tile(2 * jt + 2);
         prefetch_tile(jt + kPrefetchTiles);
     } else {
         const int P = p.P;
@@ -874,7 +881,10 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
                     l += __shfl_xor_sync(0xffffffffu, l, 4);
                     l += __shfl_xor_sync(0xffffffffu, l, 8);
                     l += __shfl_xor_sync(0xffffffffu, l, 16);
-                    const float mt = st[hh].m_true[nt][col];
+                    float mt = st[hh].m_true[nt][col];
+                    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
+                    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
+                    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
                     const float f = (mt == -INFINITY) ? 0.0f : ex2(st[hh].m_used[nt][col] - mt);
                     l_all[nt][col] = l * f;
                     m_all[nt][col] = mt;
