@@ -673,21 +673,26 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
     int4* recs = reinterpret_cast<int4*>(smem);  // this CTA's segment records (plan)
     int32_t* spids = reinterpret_cast<int32_t*>(smem + kRecCache * 32);  // first segment's page ids (plan)
 
-    if (p.status && (*(volatile int32_t*)p.status & (MG_DEV_OUT_OF_PAGES | MG_DEV_BLOCK_TABLE_FULL))) return;
-
     // ---- this CTA's segments from the step's plan: the first kPlanInline in one
-    // round trip, more (stream-K over many short sequences) from the flat array --
+    // round trip, more (stream-K over many short sequences) from the flat array.
+    // The status word, the plan header and the CTA's counts are read in the same
+    // round trip (all lie inside buffers the host sized); a step whose allocation
+    // failed then runs no segment and writes nothing. ------------------------------
     const int4* prec = reinterpret_cast<const int4*>(p.plan + p.lay.off_recs) + static_cast<int64_t>(cta) * kPlanInline * 2;
     if (tid < 2 * kPlanInline) recs[tid] = __ldcg(prec + tid);
     const int4* ppid = reinterpret_cast<const int4*>(p.plan + p.lay.off_pids) + static_cast<int64_t>(cta) * (kPlanPids / 4);
     if (tid >= 32 && tid < 32 + kPlanPids / 4) reinterpret_cast<int4*>(spids)[tid - 32] = __ldcg(ppid + tid - 32);
     if (tid == 0) {
-        const bool ok = p.plan[0] == kPlanMagic && p.plan[1] == p.batch && p.plan[2] == static_cast<int>(gridDim.x) &&
-                        p.plan[8] == p.has_staging;
-        if (!ok) flag(p.status, MG_DEV_BAD_ARGUMENT);
-        sm_hdr[0] = ok ? p.plan[p.lay.off_counts + cta] : 0;
-        sm_hdr[1] = ok ? p.plan[4] : 0;
-        sm_hdr[2] = ok ? p.plan[p.lay.off_offs + cta] : 0;
+        const int32_t stat = p.status ? *(volatile int32_t*)p.status : 0;
+        const int32_t h0 = __ldcg(p.plan), h1 = __ldcg(p.plan + 1), h2 = __ldcg(p.plan + 2), h4 = __ldcg(p.plan + 4);
+        const int32_t h8 = __ldcg(p.plan + 8);
+        const int32_t cnt = __ldcg(p.plan + p.lay.off_counts + cta), off = __ldcg(p.plan + p.lay.off_offs + cta);
+        const bool stop = (stat & (MG_DEV_OUT_OF_PAGES | MG_DEV_BLOCK_TABLE_FULL)) != 0;
+        const bool ok = h0 == kPlanMagic && h1 == p.batch && h2 == static_cast<int>(gridDim.x) && h8 == p.has_staging;
+        if (!ok && !stop) flag(p.status, MG_DEV_BAD_ARGUMENT);
+        sm_hdr[0] = (ok && !stop) ? cnt : 0;
+        sm_hdr[1] = (ok && !stop) ? h4 : 0;
+        sm_hdr[2] = (ok && !stop) ? off : 0;
     }
     __syncthreads();
     const int nseg = sm_hdr[0];

@@ -14,6 +14,7 @@ namespace {
 
 constexpr int kPlanThreads = 1024;
 constexpr int kAppendThreads = 256;
+constexpr int kKeep = 8;  // groups of 8 elements a commit thread keeps in registers
 constexpr int kGatherThreads = 256;
 
 __global__ void alloc_init_kernel(int32_t* free_stack, int32_t* n_free, int32_t* in_use, int64_t n) {
@@ -228,8 +229,10 @@ template <bool INT4, typename ST, typename NT>
 __global__ void __launch_bounds__(kAppendThreads) kv_append_kernel(AppendParams p) {
     __shared__ float red[32];
     const int b = blockIdx.x, jj = blockIdx.y, kv = blockIdx.z;
-    if (p.status && (*(volatile int32_t*)p.status & kStopBits)) return;
+    // status, length and count in one round trip
+    const int32_t stat = p.status ? *(volatile int32_t*)p.status : 0;
     const int new_len = p.seq_lens[b], add = p.n_new[b];
+    if (stat & kStopBits) return;
     if (add <= 0) return;
     if (add > p.max_new || add > new_len) {
         if (jj == 0 && kv == 0 && threadIdx.x == 0) flag(p.status, MG_DEV_BAD_ARGUMENT);
@@ -245,6 +248,14 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_kernel(AppendParams 
     const NT* src_new = static_cast<const NT*>(kv ? p.v_new : p.k_new) + static_cast<int64_t>(b) * p.max_new * row;
     const int page_start = j * P;
 
+    // 8 consecutive elements at element e of page j: staged rows, then this step's tokens
+    auto load8 = [&](int64_t e, float (&v)[8]) {
+        const int t = static_cast<int>(e / row);
+        const int tok = page_start + t;
+        const int64_t c = e - static_cast<int64_t>(t) * row;
+        if (tok < old) Vec8<ST>::load(staging + static_cast<int64_t>(t) * row + c, v);
+        else Vec8<NT>::load(src_new + static_cast<int64_t>(tok - old) * row + c, v);
+    };
     if (page_start + P <= new_len) {  // page j fills during this step: commit it
         const int32_t page = j < p.max_blocks ? p.block_tables[static_cast<int64_t>(b) * p.max_blocks + j] : -1;
         uint8_t* pool = static_cast<uint8_t*>(kv ? p.v_pool : p.k_pool);
@@ -258,40 +269,61 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_kernel(AppendParams 
             // thread runs every round, so the shuffles never diverge)
             const int gl = p.D >> 3;
             uint8_t* base = pool + static_cast<int64_t>(page) * (INT4 ? pe / 2 : pe);
-            for (int64_t r0 = 0; r0 < pe; r0 += kAppendThreads * 8) {
-                const int64_t e = r0 + threadIdx.x * 8;
-                const bool ok = e < pe;
-                const int t = ok ? static_cast<int>(e / row) : 0;
-                const int tok = page_start + t;
-                const int64_t c = e - static_cast<int64_t>(t) * row;
-                float v[8];
+            for (int64_t r0 = 0; r0 < pe; r0 += static_cast<int64_t>(kAppendThreads) * 8 * kKeep) {
+                float v[kKeep][8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) v[i] = 0.0f;
-                if (ok) {
-                    if (tok < old) Vec8<ST>::load(staging + static_cast<int64_t>(t) * row + c, v);
-                    else Vec8<NT>::load(src_new + static_cast<int64_t>(tok - old) * row + c, v);
+                for (int u = 0; u < kKeep; ++u) {
+                    const int64_t e = r0 + (static_cast<int64_t>(u) * kAppendThreads + threadIdx.x) * 8;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) v[u][i] = 0.0f;
+                    if (e < pe) load8(e, v[u]);
                 }
-                float a = 0.0f;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) a = fmaxf(a, fabsf(v[i]));
-                for (int o = gl >> 1; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-                if (ok) {
-                    const float sf = static_cast<float>(scale_from_absmax(a, INT4 ? 7.0 : 127.0));
-                    if ((threadIdx.x & (gl - 1)) == 0)
-                        scales[(static_cast<int64_t>(page) * P + t) * (row / p.D) + c / p.D] = sf;
-                    store_codes<INT4>(base, e, v, sf);
+                for (int u = 0; u < kKeep; ++u) {
+                    const int64_t e = r0 + (static_cast<int64_t>(u) * kAppendThreads + threadIdx.x) * 8;
+                    float a = 0.0f;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) a = fmaxf(a, fabsf(v[u][i]));
+                    for (int o = gl >> 1; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+                    if (e < pe) {
+                        const int t = static_cast<int>(e / row);
+                        const int64_t c = e - static_cast<int64_t>(t) * row;
+                        const float sf = static_cast<float>(scale_from_absmax(a, INT4 ? 7.0 : 127.0));
+                        if ((threadIdx.x & (gl - 1)) == 0)
+                            scales[(static_cast<int64_t>(page) * P + t) * (row / p.D) + c / p.D] = sf;
+                        store_codes<INT4>(base, e, v[u], sf);
+                    }
                 }
             }
+        } else if (pe <= static_cast<int64_t>(kAppendThreads) * 8 * kKeep) {
+            // the whole page in registers (up to kKeep groups of 8 per thread): every
+            // load in flight at once, one pass over the staged and new rows
+            float v[kKeep][8];
+            float a = 0.0f;
+#pragma unroll
+            for (int u = 0; u < kKeep; ++u) {
+                const int64_t e = (static_cast<int64_t>(u) * kAppendThreads + threadIdx.x) * 8;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[u][i] = 0.0f;
+                if (e < pe) load8(e, v[u]);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) a = fmaxf(a, fabsf(v[u][i]));
+            }
+            a = block_max(a, red);
+            const float sf = static_cast<float>(scale_from_absmax(a, INT4 ? 7.0 : 127.0));
+            if (threadIdx.x == 0) scales[page] = sf;
+            uint8_t* base = pool + static_cast<int64_t>(page) * (INT4 ? pe / 2 : pe);
+#pragma unroll
+            for (int u = 0; u < kKeep; ++u) {
+                const int64_t e = (static_cast<int64_t>(u) * kAppendThreads + threadIdx.x) * 8;
+                if (e < pe) store_codes<INT4>(base, e, v[u], sf);
+            }
         } else {
-            // element e of the page: token t = e / row
+            // larger pages: absmax pass, then a second pass that quantizes
             float a = 0.0f;
             for (int64_t e = threadIdx.x * 8; e < pe; e += kAppendThreads * 8) {
-                const int t = static_cast<int>(e / row);
-                const int tok = page_start + t;
-                const int64_t c = e - static_cast<int64_t>(t) * row;
                 float v[8];
-                if (tok < old) Vec8<ST>::load(staging + static_cast<int64_t>(t) * row + c, v);
-                else Vec8<NT>::load(src_new + static_cast<int64_t>(tok - old) * row + c, v);
+                load8(e, v);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) a = fmaxf(a, fabsf(v[i]));
             }
@@ -301,12 +333,8 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_kernel(AppendParams 
             if (threadIdx.x == 0) scales[page] = sf;
             uint8_t* base = pool + static_cast<int64_t>(page) * (INT4 ? pe / 2 : pe);
             for (int64_t e = threadIdx.x * 8; e < pe; e += kAppendThreads * 8) {
-                const int t = static_cast<int>(e / row);
-                const int tok = page_start + t;
-                const int64_t c = e - static_cast<int64_t>(t) * row;
                 float v[8];
-                if (tok < old) Vec8<ST>::load(staging + static_cast<int64_t>(t) * row + c, v);
-                else Vec8<NT>::load(src_new + static_cast<int64_t>(tok - old) * row + c, v);
+                load8(e, v);
                 store_codes<INT4>(base, e, v, sf);
             }
         }

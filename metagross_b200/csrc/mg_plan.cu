@@ -248,12 +248,25 @@ __global__ void __launch_bounds__(kPlanThreads, 1) decode_plan_kernel(const Plan
     __syncthreads();
     // ---- page ids of each CTA's first kPlanPids pages (its first segment), so an
     // attention launch starts loading pages without a block-table round trip ------
-    for (int i = threadIdx.x; i < G * kPlanPids; i += blockDim.x) {
-        const int c = i / kPlanPids, k = i - c * kPlanPids;
-        int32_t pid = 0;
-        if (k < first[3 * c + 2])
-            pid = pp.block_tables[static_cast<int64_t>(first[3 * c]) * pp.max_blocks + first[3 * c + 1] + k];
-        pp.plan[pp.lay.off_pids + i] = pid;
+    // (kBatch independent block-table loads in flight per thread before the stores)
+    constexpr int kBatch = 8;
+    for (int base = 0; base < G * kPlanPids; base += kBatch * blockDim.x) {
+        int32_t pid[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int i = base + u * blockDim.x + threadIdx.x;
+            pid[u] = 0;
+            if (i < G * kPlanPids) {
+                const int c = i / kPlanPids, k = i - c * kPlanPids;
+                if (k < first[3 * c + 2])
+                    pid[u] = pp.block_tables[static_cast<int64_t>(first[3 * c]) * pp.max_blocks + first[3 * c + 1] + k];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int i = base + u * blockDim.x + threadIdx.x;
+            if (i < G * kPlanPids) pp.plan[pp.lay.off_pids + i] = pid[u];
+        }
     }
     if (threadIdx.x == 0) {
         int32_t* h = pp.plan;
