@@ -102,6 +102,23 @@ def append_bytes(lens_after, w):
     return tot
 
 
+def append_sweep_bytes(old_lens, new_lens, w):
+    """Bytes one append launch must move for a step of any size: the new tokens
+    (K+V fp16) read once; every page that fills writes its codes (K+V) and two
+    scales and reads the rows it had staged before the step; the step's tokens of
+    the page left partial are written to staging."""
+    bq = 1.0 if w["kv"] == "int8" else 0.5
+    P, row = w["page"], w["hkv"] * w["d"]
+    tot = 0.0
+    for o, n in zip(old_lens, new_lens):
+        commits = n // P - o // P
+        tot += 2 * (n - o) * row * 2
+        if commits > 0:
+            tot += commits * (2 * P * row * bq + 8) + 2 * (o % P) * row * 2
+        tot += 2 * (n - max(o, (n // P) * P)) * row * 2
+    return tot
+
+
 # --------------------------------------------------------------------------
 # clocks sampling during the timed region
 # --------------------------------------------------------------------------
@@ -332,6 +349,94 @@ def traffic_per_launch(workload):
     return None
 
 
+def append_sweep(device, kv="int4", batch=64, sizes=(1, 4, 16, 64, 256, 1024, 4096)):
+    """KV-append bandwidth of the sharded configuration's shape (TinyLlama
+    attention shape, INT4, page 16, 64 sequences) for N new tokens per sequence
+    per step: per N, a fresh cache, 2 warm-up steps, then timed steps of one
+    allocation launch (begin_step) and one layer's append, CUDA events around
+    the steps.  N counts tokens per sequence (N x 64 tokens a step)."""
+    from metagross_b200.batched import BatchedPagedKVCache
+
+    w = dict(WORKLOADS["lognormal_int4"], kv=kv)
+    P, hkv, d = w["page"], w["hkv"], w["d"]
+    rows = []
+    for n in sizes:
+        steps = max(5, min(200, 20000 // n))
+        warm = 2
+        total = (steps + warm) * n
+        mb = total // P + 2
+        cache = BatchedPagedKVCache(1, batch, hkv, d, page_size=P, num_pages=batch * mb, max_blocks=mb, kv_dtype=kv,
+                                    staging_dtype=torch.float16, device=device)
+        g = torch.Generator(device=device).manual_seed(n)
+        k = torch.randn(batch, n, hkv, d, generator=g, device=device, dtype=torch.float16)
+        v = torch.randn(batch, n, hkv, d, generator=g, device=device, dtype=torch.float16)
+        for _ in range(warm):
+            cache.begin_step(n)
+            cache.append(0, k, v)
+        torch.cuda.synchronize()
+        cache.check()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            cache.begin_step(n)
+            cache.append(0, k, v)
+        e1.record()
+        torch.cuda.synchronize()
+        cache.check()
+        ms = e0.elapsed_time(e1) / steps
+        byts = 0.0
+        for s_ in range(steps):
+            o = (warm + s_) * n
+            byts += append_sweep_bytes([o] * batch, [o + n] * batch, w)
+        byts /= steps
+        rows.append({"n_new": n, "tokens_per_step": n * batch, "ms_per_step": round(ms, 4),
+                     "gbs": round(byts / (ms / 1e3) / 1e9, 1), "bytes_per_step": int(byts)})
+        del cache, k, v
+        torch.cuda.empty_cache()
+    return {"metric": "kv append GB/s (N new tokens per sequence per step)", "unit": "GB/s", "kv": kv,
+            "config": {"batch": batch, "num_kv_heads": hkv, "head_dim": d, "page": P,
+                       "interpretation": "N counts new tokens per sequence; one layer's append + the allocation "
+                                         "launch per step, graph-free eager launches"},
+            "sweep": rows}
+
+
+def decode_model(device, batch=64, prompt_len=128, new_tokens=256, kv="int8"):
+    """End-to-end greedy decode of the TinyLlama-1.1B architecture (22 layers,
+    hidden 2048, 32 q / 4 kv heads, FFN 5632, vocab 32000, rotary, fp16) with
+    seeded random weights on the batched paged cache: prompts of prompt_len
+    seeded random token ids, new_tokens tokens per sequence, one CUDA-graph
+    decode step per token.  A first pass warms up (cuBLAS, graph upload); the
+    cache is reset and the same prompts run again, timed with CUDA events."""
+    from metagross_b200.llama import TINYLLAMA_1_1B, LlamaDecoder
+
+    dec = LlamaDecoder(TINYLLAMA_1_1B, batch, prompt_len + new_tokens + 16, kv_dtype=kv, device=device, seed=1234)
+    g = torch.Generator().manual_seed(1234)
+    prompt = torch.randint(0, TINYLLAMA_1_1B.vocab, (batch, prompt_len), generator=g).to(device)
+    dec.prefill(prompt)
+    dec.capture()
+    dec.decode(8)
+    torch.cuda.synchronize()
+    dec.cache.reset()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    ev[0].record()
+    dec.prefill(prompt)
+    ev[1].record()
+    toks = dec.decode(new_tokens)
+    ev[2].record()
+    torch.cuda.synchronize()
+    dec.cache.check()
+    pre_ms, dec_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+    steps = new_tokens - 1  # the first new token comes out of the prefill
+    return {"metric": "decode tokens/s", "value": round(batch * steps / (dec_ms / 1e3), 1), "unit": "tokens/s",
+            "higher_is_better": True, "dtype": "fp16 model, " + kv + " paged cache", "data": "synthetic",
+            "config": {"model": "TinyLlama-1.1B architecture, seeded random weights", "batch": batch,
+                       "prompt_len": prompt_len, "new_tokens": new_tokens, "page": 16},
+            "decode_ms": round(dec_ms, 2), "ms_per_token_step": round(dec_ms / steps, 4),
+            "prefill_ms": round(pre_ms, 2),
+            "tokens_per_s_with_prefill": round(batch * new_tokens / ((pre_ms + dec_ms) / 1e3), 1),
+            "first_tokens": toks[0, :8].tolist()}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -344,7 +449,21 @@ def main():
     ap.add_argument("--layers", type=int, default=None,
                     help="override the workload's layer count (a small case for profiling; the default run uses "
                          "the workload's own depth)")
+    ap.add_argument("--append-sweep", action="store_true",
+                    help="instead of the decode benchmark, print the KV-append bandwidth sweep (1..4096 new tokens "
+                         "per sequence per step, 64 sequences, INT4) as one JSON line")
+    ap.add_argument("--decode-model", action="store_true",
+                    help="instead of the decode benchmark, print the end-to-end TinyLlama-architecture greedy decode "
+                         "throughput (batch 64, 128-token prompts, 256 new tokens, INT8 cache) as one JSON line")
+    ap.add_argument("--new-tokens", type=int, default=256, help="tokens per sequence for --decode-model")
     args = ap.parse_args()
+    if args.decode_model:
+        print(json.dumps(decode_model(torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))),
+                                      new_tokens=args.new_tokens)))
+        return
+    if args.append_sweep:
+        print(json.dumps(append_sweep(torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))))))
+        return
     w = dict(WORKLOADS[args.workload])
     if args.layers is not None:
         if args.layers < 1:

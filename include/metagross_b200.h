@@ -298,6 +298,28 @@ MG_API mg_status mg_truncate_sequences(const mg_allocator* alloc, const int32_t*
                                        int32_t num_seqs, int32_t page_size, int32_t* dev_status,
                                        mg_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Dense-side helpers of a Llama decode step (fp16 storage, fp32 math).  No
+ * counterpart among the reference's ops: they stand for the reference model's
+ * Hugging Face modules (LlamaRMSNorm, the rotate-half rotary embedding of
+ * metagross/generate_llama.py:20-37, the SiLU-gated MLP) in the batched decode
+ * loop, one launch each instead of chains of small torch kernels.
+ * ---------------------------------------------------------------------- */
+
+/* y[r, :] = fp16(x[r, :] * rsqrt(mean(x[r, :]^2) + eps)) * w, rows x cols. */
+MG_API mg_status mg_rmsnorm_f16(const void* x, const void* w, void* y, int64_t rows, int64_t cols, float eps,
+                                mg_stream_t stream);
+
+/* qkv [batch, (Hq + 2 Hkv) * D] (q | k | v heads) -> q [batch, Hq, D] and
+ * k [batch, Hkv, D] rotated at position pos[b] by the tables cos / sin
+ * [positions, D / 2] (pairs d, d + D/2), v [batch, Hkv, D] copied. */
+MG_API mg_status mg_rope_qkv_f16(const void* qkv, const int64_t* pos, const float* cos_table,
+                                 const float* sin_table, void* q, void* k, void* v, int32_t batch,
+                                 int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, mg_stream_t stream);
+
+/* h[r, j] = fp16(silu(gu[r, j])) * gu[r, ffn + j], gu [rows, 2 ffn]. */
+MG_API mg_status mg_silu_mul_f16(const void* gu, void* h, int64_t rows, int64_t ffn, mg_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -521,6 +521,63 @@ void gather_dequant(torch::Tensor k_pool, torch::Tensor v_pool, torch::Tensor k_
 
 }  // namespace
 
+// ---------------------------------------------------------------------------
+// dense-side helpers of a Llama decode step (fp16)
+// ---------------------------------------------------------------------------
+
+void check_f16_cuda(const torch::Tensor& t, const char* what) {
+    TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kFloat16 && t.is_contiguous(), what,
+                " must be a contiguous CUDA float16 tensor");
+}
+
+torch::Tensor rmsnorm(torch::Tensor x, torch::Tensor w, double eps) {
+    const c10::cuda::CUDAGuard guard(x.device());
+    check_f16_cuda(x, "x");
+    check_f16_cuda(w, "w");
+    TORCH_CHECK(w.dim() == 1 && x.size(-1) == w.size(0), "w must be [x.shape[-1]]");
+    auto y = torch::empty_like(x);
+    const int64_t cols = x.size(-1);
+    check_status(mg_rmsnorm_f16(x.data_ptr(), w.data_ptr(), y.data_ptr(), x.numel() / cols, cols,
+                                static_cast<float>(eps), cur_stream()),
+                 "rmsnorm");
+    return y;
+}
+
+void rope_qkv(torch::Tensor qkv, torch::Tensor pos, torch::Tensor cos_table, torch::Tensor sin_table,
+              torch::Tensor q, torch::Tensor k, torch::Tensor v) {
+    const c10::cuda::CUDAGuard guard(qkv.device());
+    check_f16_cuda(qkv, "qkv");
+    check_f16_cuda(q, "q");
+    check_f16_cuda(k, "k");
+    check_f16_cuda(v, "v");
+    TORCH_CHECK(q.dim() == 3 && k.dim() == 3 && v.sizes() == k.sizes(), "q [B, Hq, D], k / v [B, Hkv, D]");
+    const int64_t B = q.size(0), Hq = q.size(1), D = q.size(2), Hkv = k.size(1);
+    TORCH_CHECK(qkv.dim() == 2 && qkv.size(0) == B && qkv.size(1) == (Hq + 2 * Hkv) * D, "qkv must be [B, (Hq + 2 Hkv) D]");
+    TORCH_CHECK(pos.is_cuda() && pos.scalar_type() == torch::kInt64 && pos.numel() == B && pos.is_contiguous(),
+                "pos must be a contiguous CUDA int64 [B] tensor");
+    TORCH_CHECK(cos_table.is_cuda() && cos_table.scalar_type() == torch::kFloat32 && cos_table.is_contiguous() &&
+                    cos_table.dim() == 2 && cos_table.size(1) == D / 2 && sin_table.sizes() == cos_table.sizes() &&
+                    sin_table.is_contiguous() && sin_table.scalar_type() == torch::kFloat32,
+                "cos / sin tables must be contiguous CUDA float32 [positions, D / 2]");
+    check_status(mg_rope_qkv_f16(qkv.data_ptr(), pos.data_ptr<int64_t>(), cos_table.data_ptr<float>(),
+                                 sin_table.data_ptr<float>(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                 static_cast<int32_t>(B), static_cast<int32_t>(Hq), static_cast<int32_t>(Hkv),
+                                 static_cast<int32_t>(D), cur_stream()),
+                 "rope_qkv");
+}
+
+torch::Tensor silu_mul(torch::Tensor gu) {
+    const c10::cuda::CUDAGuard guard(gu.device());
+    check_f16_cuda(gu, "gu");
+    TORCH_CHECK(gu.size(-1) % 2 == 0, "gu's last dimension must be even (gate | up)");
+    const int64_t F = gu.size(-1) / 2;
+    auto shape = gu.sizes().vec();
+    shape.back() = F;
+    auto h = torch::empty(shape, gu.options());
+    check_status(mg_silu_mul_f16(gu.data_ptr(), h.data_ptr(), gu.numel() / (2 * F), F, cur_stream()), "silu_mul");
+    return h;
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.doc() = "B200-native paged quantized KV-cache ops (C ABI: libmgb200.so)";
     m.def("add", &add, "Elementwise add of two CUDA float32 tensors (build sanity check)");
@@ -573,5 +630,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           pybind11::arg("staging_k"), pybind11::arg("staging_v"), pybind11::arg("block_tables"),
           pybind11::arg("seq_lens"), pybind11::arg("cu_seqlens"), pybind11::arg("max_context"),
           pybind11::arg("out_k"), pybind11::arg("out_v"), pybind11::arg("status") = pybind11::none());
+    m.def("rmsnorm", &rmsnorm, "RMSNorm over the last dimension (fp16, fp32 math)", pybind11::arg("x"),
+          pybind11::arg("w"), pybind11::arg("eps"));
+    m.def("rope_qkv", &rope_qkv, "Split q | k | v, rotary embedding of q and k at per-row positions",
+          pybind11::arg("qkv"), pybind11::arg("pos"), pybind11::arg("cos_table"), pybind11::arg("sin_table"),
+          pybind11::arg("q"), pybind11::arg("k"), pybind11::arg("v"));
+    m.def("silu_mul", &silu_mul, "silu(gate) * up of a [.., 2F] gate | up tensor", pybind11::arg("gu"));
     m.def("version", []() { return std::string(mg_version()); });
 }

@@ -7,6 +7,8 @@
 // and every layer (all layers commit at the same token counts, so one block
 // table per sequence serves them all -- the reference's 2*num_layers
 // allocators of one sequence all hand out the same ids).
+#include <type_traits>
+
 #include "mg_common.cuh"
 
 namespace mg {
@@ -14,7 +16,6 @@ namespace {
 
 constexpr int kPlanThreads = 1024;
 constexpr int kAppendThreads = 256;
-constexpr int kKeep = 8;  // groups of 8 elements a commit thread keeps in registers
 constexpr int kGatherThreads = 256;
 
 __global__ void alloc_init_kernel(int32_t* free_stack, int32_t* n_free, int32_t* in_use, int64_t n) {
@@ -225,8 +226,11 @@ __device__ __forceinline__ void store_codes(uint8_t* page_base, int64_t e, const
     }
 }
 
-template <bool INT4, typename ST, typename NT>
-__global__ void __launch_bounds__(kAppendThreads) kv_append_kernel(AppendParams p) {
+// KEEP: groups of 8 elements a commit thread keeps in registers (2 for pages of
+// up to 4096 elements, which then leaves room for 4 CTAs per SM; 8 otherwise).
+template <bool INT4, typename ST, typename NT, int KEEP>
+__global__ void __launch_bounds__(kAppendThreads, KEEP <= 2 ? 4 : 2) kv_append_kernel(AppendParams p) {
+    constexpr int kKeep = KEEP;
     __shared__ float red[32];
     const int b = blockIdx.x, jj = blockIdx.y, kv = blockIdx.z;
     // status, length and count in one round trip
@@ -552,12 +556,18 @@ extern "C" mg_status mg_kv_append(const mg_cache_layout* L, const mg_layer_ptrs*
     const bool i4 = L->kv_dtype == MG_KV_INT4;
     const bool s16 = L->staging_dtype == MG_F16, n16 = new_dtype == MG_F16;
     cudaStream_t s = as_stream(stream);
-    if (!i4 && s16 && n16) kv_append_kernel<false, __half, __half><<<grid, kAppendThreads, 0, s>>>(p);
-    else if (!i4 && !s16 && n16) kv_append_kernel<false, float, __half><<<grid, kAppendThreads, 0, s>>>(p);
-    else if (!i4 && !s16 && !n16) kv_append_kernel<false, float, float><<<grid, kAppendThreads, 0, s>>>(p);
-    else if (i4 && s16 && n16) kv_append_kernel<true, __half, __half><<<grid, kAppendThreads, 0, s>>>(p);
-    else if (i4 && !s16 && n16) kv_append_kernel<true, float, __half><<<grid, kAppendThreads, 0, s>>>(p);
-    else kv_append_kernel<true, float, float><<<grid, kAppendThreads, 0, s>>>(p);
+    const bool small = static_cast<int64_t>(L->page_size) * p.row <= static_cast<int64_t>(kAppendThreads) * 8 * 2;
+    auto go = [&](auto keep) {
+        constexpr int K = decltype(keep)::value;
+        if (!i4 && s16 && n16) kv_append_kernel<false, __half, __half, K><<<grid, kAppendThreads, 0, s>>>(p);
+        else if (!i4 && !s16 && n16) kv_append_kernel<false, float, __half, K><<<grid, kAppendThreads, 0, s>>>(p);
+        else if (!i4 && !s16 && !n16) kv_append_kernel<false, float, float, K><<<grid, kAppendThreads, 0, s>>>(p);
+        else if (i4 && s16 && n16) kv_append_kernel<true, __half, __half, K><<<grid, kAppendThreads, 0, s>>>(p);
+        else if (i4 && !s16 && n16) kv_append_kernel<true, float, __half, K><<<grid, kAppendThreads, 0, s>>>(p);
+        else kv_append_kernel<true, float, float, K><<<grid, kAppendThreads, 0, s>>>(p);
+    };
+    if (small) go(std::integral_constant<int, 2>{});
+    else go(std::integral_constant<int, 8>{});
     return check_launch("kv_append_kernel");
 }
 
