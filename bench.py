@@ -400,6 +400,50 @@ def append_sweep(device, kv="int4", batch=64, sizes=(1, 4, 16, 64, 256, 1024, 40
             "sweep": rows}
 
 
+def gather_bench(device, workload="tinyllama_int4", reps=20):
+    """The standalone block gather + dequantize (one layer pool of the named
+    workload, every sequence, fp16 out): device GB/s over the bytes it must
+    move (codes + page scales + block-table entries + staged rows read, fp16
+    K/V written), CUDA events over reps launches."""
+    from metagross_b200 import _C
+
+    w = dict(WORKLOADS[workload], layers=1)
+    cache, _, _, _, _, _, _ = build(w, device, seed=4321)
+    lens = cache.seq_lens.cpu()
+    cu = torch.zeros(cache.batch + 1, dtype=torch.int32)
+    cu[1:] = torch.cumsum(lens, 0)
+    total = int(cu[-1])
+    ok = torch.empty(total, cache.num_kv_heads, cache.head_dim, dtype=torch.float16, device=device)
+    ov = torch.empty_like(ok)
+    cu_d = cu.to(device)
+    mc = int(lens.max())
+
+    def run():
+        _C.gather_dequant(cache.k_pool[0], cache.v_pool[0], cache.k_scales[0], cache.v_scales[0], cache.staging_k[0],
+                          cache.staging_v[0], cache.block_tables, cache.seq_lens, cu_d, mc, ok, ov, cache.status)
+
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    cache.check()
+    ms = e0.elapsed_time(e1) / reps
+    bq = 1.0 if w["kv"] == "int8" else 0.5
+    P, row = w["page"], w["hkv"] * w["d"]
+    byts = 0.0
+    for c in lens.tolist():
+        n, r = c // P, c % P
+        byts += 2 * n * P * row * bq + 8 * n + 4 * n + 2 * r * row * 2 + 2 * c * row * 2
+    return {"metric": "gather + dequantize GB/s", "value": round(byts / (ms / 1e3) / 1e9, 1), "unit": "GB/s",
+            "workload": workload, "sequences": cache.batch, "tokens": total, "ms_per_launch": round(ms, 4),
+            "bytes_per_launch": int(byts)}
+
+
 def decode_model(device, batch=64, prompt_len=128, new_tokens=256, kv="int8"):
     """End-to-end greedy decode of the TinyLlama-1.1B architecture (22 layers,
     hidden 2048, 32 q / 4 kv heads, FFN 5632, vocab 32000, rotary, fp16) with
@@ -456,13 +500,22 @@ def main():
                     help="instead of the decode benchmark, print the end-to-end TinyLlama-architecture greedy decode "
                          "throughput (batch 64, 128-token prompts, 256 new tokens, INT8 cache) as one JSON line")
     ap.add_argument("--new-tokens", type=int, default=256, help="tokens per sequence for --decode-model")
+    ap.add_argument("--sweep-sizes", default="1,4,16,64,256,1024,4096",
+                    help="new tokens per sequence for --append-sweep (comma-separated)")
+    ap.add_argument("--gather", action="store_true",
+                    help="instead of the decode benchmark, print the gather + dequantize bandwidth on one layer pool "
+                         "of --workload as one JSON line")
     args = ap.parse_args()
+    if args.gather:
+        print(json.dumps(gather_bench(torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))), args.workload)))
+        return
     if args.decode_model:
         print(json.dumps(decode_model(torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))),
                                       new_tokens=args.new_tokens)))
         return
     if args.append_sweep:
-        print(json.dumps(append_sweep(torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))))))
+        print(json.dumps(append_sweep(torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))),
+                                      sizes=tuple(int(x) for x in args.sweep_sizes.split(",")))))
         return
     w = dict(WORKLOADS[args.workload])
     if args.layers is not None:
