@@ -583,12 +583,13 @@ __device__ __forceinline__ uint32_t ticket_add(uint32_t* t) {
 // The last CTA to finish (sequence b, kv head h) merges the partials of all
 // pieces of the sequence (slots pbase .. pbase + ncov - 1; log-sum-exp, one
 // pass, four partials per load round) and writes the outputs of the head's
-// G query heads; one warp.
+// G query heads; the wph warps of the head take alternate 32-column groups.
 template <int HD>
-__device__ __forceinline__ void merge_partials(const DecodeParams& p, int b, int h, int pbase, int ncov, int lane) {
+__device__ __forceinline__ void merge_partials(const DecodeParams& p, int b, int h, int pbase, int ncov, int lane,
+                                               int wsub, int wph) {
     constexpr float kLn2 = 0.6931471805599453f;
     const int Hq = p.Hq;
-    for (int it = lane; it < p.G * (HD / 4); it += 32) {
+    for (int it = wsub * 32 + lane; it < p.G * (HD / 4); it += wph * 32) {
         const int gq = it / (HD / 4), d4 = (it - gq * (HD / 4)) * 4;
         const int hq = h * p.G + gq;
         float M = -INFINITY, L = 0.0f;
@@ -659,6 +660,7 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
     constexpr float kLn2 = 0.6931471805599453f;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int sm_hdr[3];
+    __shared__ int sm_last[2 * 2 * kWarps];  // (cut segment, head of the warp, kv-head group): this CTA merges
 
     grid_dependency_wait();
     grid_launch_dependents();
@@ -844,6 +846,7 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
     for (int cidx = 0; cidx < nseg; ++cidx) {
         const Segment sc = make_segment(rec(cidx), p.P, wsub, WPH, nh, tt, tc);
         const int b = sc.b;
+        if (!sc.complete) pend_s[cidx == 0 ? 0 : 1] = cidx;  // every warp: the cut segments are the CTA's
 #pragma unroll
         for (int hh = 0; hh < HPW; ++hh) {
             const int h = hh ? h1 : hbase;
@@ -1002,20 +1005,15 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
             __syncwarp();
             uint32_t prev = 0;
             if (lane == 0) prev = ticket_add(&p.tickets[static_cast<int64_t>(b) * Hkv + h]);
-            if (cidx == 0) {
-                pend_s[0] = cidx;
-                pend_t[0][hh] = prev;
-            } else {
-                pend_s[1] = cidx;
-                pend_t[1][hh] = prev;
-            }
+            pend_t[cidx == 0 ? 0 : 1][hh] = prev;
         }
     }
 
-    // ---- merges of the cut sequences whose last covering CTA this is ---------------
+    // ---- merges of the cut sequences whose last covering CTA this is: the warp
+    // that took the ticket tells the head's other warps, which share the merge ---
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
-        if (wsub != 0 || pend_s[k] < 0) continue;
+        if (pend_s[k] < 0) continue;
         const int4 r0 = rec(pend_s[k])[0], r1 = rec(pend_s[k])[1];
         const int b = r0.x, pbase = r1.y, ncov = r1.z;
         const uint32_t need = static_cast<uint32_t>(ncov - 1);
@@ -1023,10 +1021,17 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
         for (int hh = 0; hh < HPW; ++hh) {
             const int h = hh ? h1 : hbase;
             if (h < 0) continue;
-            const uint32_t prev = __shfl_sync(0xffffffffu, pend_t[k][hh], 0);
-            if (prev != need) continue;
+            bool last = false;
+            if (wsub == 0) last = __shfl_sync(0xffffffffu, pend_t[k][hh], 0) == need;
+            if (WPH > 1) {
+                int* slot = sm_last + (k * 2 + hh) * kWarps + hbase;
+                if (wsub == 0 && lane == 0) *slot = last ? 1 : 0;
+                named_barrier_sync(1 + hbase, WPH * 32);
+                last = *slot != 0;
+            }
+            if (!last) continue;
             __threadfence();
-            merge_partials<HD>(p, b, h, pbase, ncov, lane);
+            merge_partials<HD>(p, b, h, pbase, ncov, lane, wsub, WPH);
         }
     }
     cp_async_wait_all();  // no copy outlives the CTA
