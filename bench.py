@@ -657,12 +657,24 @@ def main():
     att_lens = timed_plans[-1][2]
     att_bytes_per_launch = attention_bytes(att_lens, w)
     del g_att
+    gather_ms = 0.0
     if world > 1:
         import torch.distributed as dist
 
-        t = torch.tensor([ms, att_avg_ms], device=device)
+        # the per-step output gather alone (NCCL over NVLink), reported beside the step
+        dist.barrier()
+        torch.cuda.synchronize()
+        g0 = torch.cuda.Event(enable_timing=True)
+        g1 = torch.cuda.Event(enable_timing=True)
+        g0.record()
+        for _ in range(20):
+            gather()
+        g1.record()
+        torch.cuda.synchronize()
+        gather_ms = g0.elapsed_time(g1) / 20
+        t = torch.tensor([ms, att_avg_ms, gather_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, att_avg_ms = float(t[0]), float(t[1])
+        ms, att_avg_ms, gather_ms = float(t[0]), float(t[1]), float(t[2])
 
     # ---- end to end through the public API with host buffers -----------------
     qh = q.cpu().pin_memory()
@@ -732,6 +744,7 @@ def main():
                          "timing": f"graph of the {L} attention launches (one per layer pool), CUDA events, "
                                    f"{att_reps} replays"},
             "e2e": e2e,
+            "gather_ms_per_step": round(gather_ms, 4) if world > 1 else None,
             "gpu_launches": args.steps * (2 + 2 * L) + n_trunc,
             "clocks": clk,
         }
