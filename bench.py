@@ -558,7 +558,7 @@ def main():
         from metagross_b200.sharding import ShardGather, lpt_shard
 
         glob_ctx = contexts_for(w, w["batch"], seed=1234)
-        shards = lpt_shard(glob_ctx.numpy(), world)
+        shards = lpt_shard(glob_ctx.numpy(), world, equal_counts=True)
         cache, sched, max_ctx, q, kn, vn, out = build(w, device, seed=1234 + rank,
                                                       ctx=glob_ctx[torch.as_tensor(shards[rank])])
         if world > 1:
@@ -581,7 +581,9 @@ def main():
             import torch.distributed as dist
 
             if gatherer is not None:
-                gatherer(out[L - 1])
+                # every rank's last-layer outputs on every rank: the padded rank-major buffer
+                # and the per-rank lengths (the global order is one index_select away)
+                gatherer(out[L - 1], reorder=False)
             else:
                 dist.all_gather_into_tensor(gather_buf, out[L - 1])
 

@@ -17,11 +17,15 @@ import numpy as np
 import torch
 
 
-def lpt_shard(lens, world: int):
+def lpt_shard(lens, world: int, equal_counts: bool = False):
     """Partition sequence indices over ``world`` ranks by total length.
 
     Returns a list of ``world`` int64 arrays (ascending indices per rank).
-    The largest rank load is at most (4/3 - 1/(3*world)) of the optimum."""
+    The largest rank load is at most (4/3 - 1/(3*world)) of the optimum.
+    ``equal_counts``: every rank also gets ceil or floor(N / world) sequences
+    (the first N % world ranks one more), so the ranks' output blocks have
+    one size and an all-gather needs no padding copy; the greedy step then
+    picks the least-loaded rank that still has room."""
     if world < 1:
         raise ValueError(f"world must be >= 1, got {world}")
     lens = np.asarray(lens, dtype=np.int64)
@@ -31,11 +35,17 @@ def lpt_shard(lens, world: int):
         raise ValueError("lengths must be non-negative")
     order = np.lexsort((np.arange(lens.size), -lens))  # longest first, index order within ties
     load = np.zeros(world, dtype=np.int64)
+    room = np.full(world, np.iinfo(np.int64).max, dtype=np.int64)
+    if equal_counts:
+        room = np.full(world, lens.size // world, dtype=np.int64)
+        room[: lens.size % world] += 1
     owner = np.empty(lens.size, dtype=np.int64)
+    big = np.iinfo(np.int64).max
     for i in order:
-        r = int(np.argmin(load))  # first minimum: the lowest rank among ties
+        r = int(np.argmin(np.where(room > 0, load, big)))  # first minimum among ranks with room
         owner[i] = r
         load[r] += lens[i]
+        room[r] -= 1
     return [np.flatnonzero(owner == r) for r in range(world)]
 
 
@@ -64,12 +74,26 @@ class ShardGather:
             src[s] = r * self.n_max + np.arange(s.size)
         self.src = torch.as_tensor(src, device=device)
 
-    def __call__(self, local_out: torch.Tensor, group=None) -> torch.Tensor:
+    def __call__(self, local_out: torch.Tensor, group=None, reorder: bool = True) -> torch.Tensor:
+        """All ranks' outputs.  reorder=True: [N, ...] in global sequence order.
+        reorder=False: the padded [world * n_max, ...] rank-major buffer itself
+        (rank r's sequences shards[r] at rows r * n_max ...; ``lengths`` gives
+        each rank's count), with no reordering pass.  A local block that
+        already has n_max contiguous rows is sent as it is, without a copy."""
         import torch.distributed as dist
 
         n_r = self.shards[self.rank].size
         if local_out.shape[0] != n_r:
             raise ValueError(f"rank {self.rank} owns {n_r} sequences, got {local_out.shape[0]} outputs")
-        self.send[:n_r].copy_(local_out)
-        dist.all_gather_into_tensor(self.recv, self.send, group=group)
-        return self.recv.index_select(0, self.src)
+        if n_r == self.n_max and local_out.is_contiguous() and local_out.dtype == self.send.dtype:
+            send = local_out
+        else:
+            self.send[:n_r].copy_(local_out)
+            send = self.send
+        dist.all_gather_into_tensor(self.recv, send, group=group)
+        return self.recv.index_select(0, self.src) if reorder else self.recv
+
+    @property
+    def lengths(self):
+        """Sequences per rank (the valid rows of each n_max block of the padded buffer)."""
+        return [int(s.size) for s in self.shards]

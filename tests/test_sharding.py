@@ -36,6 +36,18 @@ def test_lpt_is_deterministic_and_handles_small_cases():
         lpt_shard([1, -2], 2)
 
 
+def test_lpt_equal_counts_keeps_sizes_and_balance():
+    g = np.random.default_rng(5)
+    lens = g.lognormal(np.log(2048), 1.0, 1024).clip(1, 32768).astype(np.int64)
+    for world in (2, 4, 8):
+        shards = lpt_shard(lens, world, equal_counts=True)
+        assert [s.size for s in shards] == [1024 // world] * world
+        np.testing.assert_array_equal(np.sort(np.concatenate(shards)), np.arange(lens.size))
+        loads = shard_loads(lens, shards)
+        assert max(loads) / max(lens.sum() / world, lens.max()) < 1.02
+    assert [s.size for s in lpt_shard([9, 1, 1, 1, 1], 2, equal_counts=True)] == [3, 2]
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -55,6 +67,13 @@ def _gather_rank(rank, world, port, lens, q):
         # a second step through the same buffers
         out2 = gather(2 * glob[torch.as_tensor(shards[rank])])
         ok = ok and torch.equal(out2, 2 * glob)
+        # equal counts: each rank's block goes out as it is; the padded buffer in rank order
+        eq = lpt_shard(lens, world, equal_counts=True)
+        g2 = ShardGather(eq, rank, (2, 3), torch.float32, "cpu")
+        raw = g2(glob[torch.as_tensor(eq[rank])].contiguous(), reorder=False)
+        for r, sh in enumerate(eq):
+            ok = ok and torch.equal(raw[r * g2.n_max:r * g2.n_max + g2.lengths[r]], glob[torch.as_tensor(sh)])
+        ok = ok and torch.equal(g2(glob[torch.as_tensor(eq[rank])].contiguous()), glob)
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, ok))
