@@ -93,54 +93,139 @@ __global__ void __launch_bounds__(kPlanThreads) plan_append_kernel(int32_t* free
 
 // Frees the listed sequences' pages beyond new_lens (0 when new_lens is
 // null) in (list order, block-table order): the order in which the
-// reference's BlockAllocator.free would be called.
+// reference's BlockAllocator.free would be called.  One CTA.  With distinct
+// sequence ids and the bookkeeping in shared memory (sm_words > 0), every
+// listed sequence is checked at once, the pages to free are numbered by a
+// prefix sum over the list, and the whole flattened page list is freed in
+// block-wide rounds; a list that names a sequence twice takes the sequential
+// walk, which sees each entry's effect on the next.
 __global__ void __launch_bounds__(kPlanThreads) free_sequences_kernel(int32_t* free_stack, int32_t* n_free_p,
                                                                       int32_t* in_use, int64_t num_pages,
                                                                       const int32_t* block_tables,
                                                                       int32_t max_blocks, int32_t* seq_lens,
                                                                       int32_t batch, const int32_t* seq_ids,
                                                                       const int32_t* new_lens, int32_t num_seqs,
-                                                                      int32_t P, int32_t* status) {
+                                                                      int32_t P, int32_t* status, int32_t sm_words) {
+    extern __shared__ int fsm[];
     __shared__ int scratch[33];
+    __shared__ int s_dup;
     int top = *n_free_p;
-    for (int i = 0; i < num_seqs; ++i) {
-        const int s = seq_ids[i];
-        if (s < 0 || s >= batch) {
-            if (threadIdx.x == 0) flag(status, MG_DEV_BAD_ARGUMENT);
-            continue;
+    auto free_page = [&](const int32_t* row, int j, bool live, int32_t& page) -> int {
+        if (!live) return 0;
+        page = row[j];
+        if (page < 0 || page >= num_pages) {
+            flag(status, MG_DEV_BAD_PAGE_ID);
+            return 0;
         }
-        const int old_len = seq_lens[s];
-        const int new_len = new_lens ? new_lens[i] : 0;
-        const int committed = (old_len / P) * P;
-        if (new_len < 0 || new_len > old_len || (new_len % P != 0 && new_len < committed)) {
-            if (threadIdx.x == 0) flag(status, MG_DEV_BAD_ARGUMENT);
-            continue;
+        if (atomicExch(&in_use[page], 0) != 1) {
+            flag(status, MG_DEV_DOUBLE_FREE);
+            return 0;
         }
-        int npages = old_len / P;
-        if (npages > max_blocks) npages = max_blocks;
-        const int keep = new_len / P;
-        const int32_t* row = block_tables + static_cast<int64_t>(s) * max_blocks;
-        for (int start = keep; start < npages; start += blockDim.x) {
-            const int j = start + threadIdx.x;
-            int ok = 0;
-            int32_t page = -1;
-            if (j < npages) {
-                page = row[j];
-                if (page < 0 || page >= num_pages) {
-                    flag(status, MG_DEV_BAD_PAGE_ID);
-                } else if (atomicExch(&in_use[page], 0) != 1) {
-                    flag(status, MG_DEV_DOUBLE_FREE);
+        return 1;
+    };
+    bool sequential = sm_words == 0;
+    if (!sequential) {
+        int* base = fsm;                  // [num_seqs + 1] first flattened page of entry i
+        int* keep = base + num_seqs + 1;  // [num_seqs] first page freed, -1: entry skipped
+        unsigned* seen = reinterpret_cast<unsigned*>(keep + num_seqs);  // [batch / 32 + 1] bitmap
+        const int nbits = batch / 32 + 1;
+        if (threadIdx.x == 0) s_dup = 0;
+        for (int w = threadIdx.x; w < nbits; w += blockDim.x) seen[w] = 0u;
+        __syncthreads();
+        for (int i = threadIdx.x; i < num_seqs; i += blockDim.x) {
+            const int sq = seq_ids[i];
+            int cnt = 0, kp = -1;
+            if (sq < 0 || sq >= batch) {
+                flag(status, MG_DEV_BAD_ARGUMENT);
+            } else {
+                if (atomicOr(&seen[sq >> 5], 1u << (sq & 31)) & (1u << (sq & 31))) s_dup = 1;
+                const int old_len = seq_lens[sq];
+                const int new_len = new_lens ? new_lens[i] : 0;
+                const int committed = (old_len / P) * P;
+                if (new_len < 0 || new_len > old_len || (new_len % P != 0 && new_len < committed)) {
+                    flag(status, MG_DEV_BAD_ARGUMENT);
                 } else {
-                    ok = 1;
+                    const int npages = old_len / P < max_blocks ? old_len / P : max_blocks;
+                    kp = new_len / P;
+                    cnt = npages > kp ? npages - kp : 0;
                 }
             }
-            int cnt;
-            const int excl = block_exclusive_scan(ok, scratch, &cnt);
-            if (ok) free_stack[top + excl] = page;
-            top += cnt;
+            base[i] = cnt;
+            keep[i] = kp;
         }
         __syncthreads();
-        if (threadIdx.x == 0) seq_lens[s] = new_len;
+        sequential = s_dup != 0;
+        if (!sequential) {
+            // exclusive prefix of the counts, in place
+            int run = 0;
+            for (int start = 0; start < num_seqs; start += blockDim.x) {
+                const int i = start + threadIdx.x;
+                const int v = i < num_seqs ? base[i] : 0;
+                int tot;
+                const int ex = block_exclusive_scan(v, scratch, &tot);
+                __syncthreads();
+                if (i < num_seqs) base[i] = run + ex;
+                run += tot;
+                __syncthreads();
+            }
+            if (threadIdx.x == 0) base[num_seqs] = run;
+            __syncthreads();
+            const int total = run;
+            for (int t0 = 0; t0 < total; t0 += blockDim.x) {
+                const int t = t0 + threadIdx.x;
+                int ok = 0;
+                int32_t page = -1;
+                if (t < total) {
+                    int lo = 0, hi = num_seqs - 1;  // last entry i with base[i] <= t
+                    while (lo < hi) {
+                        const int mid = (lo + hi + 1) >> 1;
+                        if (base[mid] <= t) lo = mid;
+                        else hi = mid - 1;
+                    }
+                    const int32_t* row = block_tables + static_cast<int64_t>(seq_ids[lo]) * max_blocks;
+                    ok = free_page(row, keep[lo] + (t - base[lo]), true, page);
+                }
+                int cnt;
+                const int excl = block_exclusive_scan(ok, scratch, &cnt);
+                if (ok) free_stack[top + excl] = page;
+                top += cnt;
+            }
+            __syncthreads();
+            for (int i = threadIdx.x; i < num_seqs; i += blockDim.x)
+                if (keep[i] >= 0) seq_lens[seq_ids[i]] = new_lens ? new_lens[i] : 0;
+        }
+    }
+    if (sequential) {
+        for (int i = 0; i < num_seqs; ++i) {
+            const int sq = seq_ids[i];
+            if (sq < 0 || sq >= batch) {
+                if (threadIdx.x == 0) flag(status, MG_DEV_BAD_ARGUMENT);
+                continue;
+            }
+            const int old_len = seq_lens[sq];
+            const int new_len = new_lens ? new_lens[i] : 0;
+            const int committed = (old_len / P) * P;
+            if (new_len < 0 || new_len > old_len || (new_len % P != 0 && new_len < committed)) {
+                if (threadIdx.x == 0) flag(status, MG_DEV_BAD_ARGUMENT);
+                continue;
+            }
+            int npages = old_len / P;
+            if (npages > max_blocks) npages = max_blocks;
+            const int kp = new_len / P;
+            const int32_t* row = block_tables + static_cast<int64_t>(sq) * max_blocks;
+            for (int start = kp; start < npages; start += blockDim.x) {
+                const int j = start + threadIdx.x;
+                int32_t page = -1;
+                const int ok = free_page(row, j, j < npages, page);
+                int cnt;
+                const int excl = block_exclusive_scan(ok, scratch, &cnt);
+                if (ok) free_stack[top + excl] = page;
+                top += cnt;
+            }
+            __syncthreads();
+            if (threadIdx.x == 0) seq_lens[sq] = new_len;
+            __syncthreads();  // the next entry may name the same sequence
+        }
     }
     if (threadIdx.x == 0) *n_free_p = top;
 }
@@ -499,10 +584,12 @@ extern "C" mg_status mg_truncate_sequences(const mg_allocator* a, const int32_t*
     if (num_seqs == 0) return MG_OK;
     MG_REQUIRE(block_tables && seq_lens && seq_ids, "null pointer");
     MG_REQUIRE(page_size >= 1 && max_blocks >= 1 && batch >= 1, "page_size, max_blocks and batch must be positive");
-    free_sequences_kernel<<<1, kPlanThreads, 0, as_stream(stream)>>>(a->free_stack, a->n_free, a->in_use,
-                                                                     a->num_pages, block_tables, max_blocks,
-                                                                     seq_lens, batch, seq_ids, new_lens, num_seqs,
-                                                                     page_size, dev_status);
+    // shared memory of the parallel walk: prefix [n + 1], keep [n], bitmap [batch / 32 + 1]
+    const int64_t words = 2ll * num_seqs + 1 + batch / 32 + 1;
+    const bool fits = words * 4 <= 48 * 1024;
+    free_sequences_kernel<<<1, kPlanThreads, fits ? static_cast<size_t>(words * 4) : 0, as_stream(stream)>>>(
+        a->free_stack, a->n_free, a->in_use, a->num_pages, block_tables, max_blocks, seq_lens, batch, seq_ids,
+        new_lens, num_seqs, page_size, dev_status, fits ? static_cast<int32_t>(words) : 0);
     return check_launch("free_sequences_kernel");
 }
 

@@ -160,6 +160,53 @@ def test_free_and_reuse_is_lifo():
     _assert_state_equal(cache, model)
 
 
+@pytest.mark.parametrize("order", [[2, 0, 1], [1, 2, 1], [0, 5, 2]])
+def test_free_many_sequences_lifo_order(order):
+    """Several sequences freed in one call, in list order then block-table order,
+    as the reference allocator would receive them: distinct ids (the parallel
+    walk), a repeated id (the sequential walk; the second entry frees nothing)
+    and an id out of range (flagged and skipped)."""
+    B, H, D, P = 3, 2, 64, 16
+    cache = _cache_cls()(1, B, H, D, page_size=P, num_pages=24, max_blocks=8)
+    model = O.PagedCacheModel(B, 24, P, H, D, staging_dtype=np.float16, max_blocks=8)
+    g = torch.Generator().manual_seed(2)
+    lens = torch.tensor([70, 33, 100], dtype=torch.int32)
+    k = torch.randn(B, 100, H, D, generator=g).half()
+    cache.begin_step(lens)
+    cache.append(0, k.cuda(), k.cuda())
+    model.append(k.numpy(), k.numpy(), lens.numpy())
+    cache.free(order)
+    for b in order:
+        if b < B:
+            model.free_sequence(b)
+    assert cache.allocator.free_list() == model.free_list
+    assert cache.seq_lens.tolist() == [int(x) for x in model.seq_lens]
+    if max(order) >= B:
+        with pytest.raises(RuntimeError, match="inconsistent per-sequence argument"):
+            cache.check()
+    else:
+        cache.check()
+
+
+def test_truncate_many_sequences_matches_oracle():
+    B, H, D, P = 6, 2, 64, 16
+    cache = _cache_cls()(1, B, H, D, page_size=P, num_pages=64, max_blocks=10)
+    model = O.PagedCacheModel(B, 64, P, H, D, staging_dtype=np.float16, max_blocks=10)
+    g = torch.Generator().manual_seed(4)
+    lens = torch.tensor([150, 16, 77, 130, 5, 64], dtype=torch.int32)
+    k = torch.randn(B, 150, H, D, generator=g).half()
+    cache.begin_step(lens)
+    cache.append(0, k.cuda(), k.cuda())
+    model.append(k.numpy(), k.numpy(), lens.numpy())
+    ids, new = [5, 0, 3, 2], [32, 80, 128, 64]
+    cache.truncate(torch.tensor(new, dtype=torch.int32), ids)
+    for b, n in zip(ids, new):
+        model.truncate(b, n)
+    cache.check()
+    assert cache.allocator.free_list() == model.free_list
+    assert cache.seq_lens.tolist() == [int(x) for x in model.seq_lens]
+
+
 def test_out_of_pages_is_all_or_nothing():
     B, H, D, P = 2, 2, 64, 16
     cache = _cache_cls()(1, B, H, D, page_size=P, num_pages=3, max_blocks=8)
