@@ -50,7 +50,7 @@
 namespace mg {
 
 constexpr int kWarps = 16;      // warps per CTA (one CTA per SM): <= 128 registers per thread
-constexpr int kWarpsDeep = 12;  // head_dim 64, one n-tile: <= 168 registers, a deeper tile ring
+constexpr int kWarpsDeep = 12;  // head_dim 64, one n-tile: <= 168 registers (room for a copy of the tile math per ring slot)
 constexpr int kWarpsWide = 8;   // head_dim 128 or two n-tiles with <= 8 kv heads: <= 255 registers
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 2^8 in fp16
 constexpr int kMetaLanes = 32;             // page ids cached per warp (one per lane)
