@@ -1,6 +1,6 @@
 """CPU baseline: the reference's CPU path for decode attention, timed.
 
-TEST / BASELINE INFRASTRUCTURE ONLY (used by bench.py's CPU-baseline leg and
+TEST / CPU-baseline infrastructure only (used by bench.py's CPU-baseline leg and
 its ``--impl reference`` arm).  It restates the reference's CPU implementation
 of the path -- tests/reference.py's dequantize (``codes.astype(float32) *
 float32(scale)`` per page; the INT4 nibble unpack of

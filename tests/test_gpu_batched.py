@@ -3,7 +3,7 @@
 Bit-exact after every step: pools (INT8 codes / packed INT4 nibbles), page
 scales, block tables (LIFO allocator order), sequence lengths, staged rows.
 Attention: max-abs within 2e-3 of float64 dequantize-then-attend for fp16
-outputs, 1e-3 for fp32.  The gather/dequantize kernel is
+outputs (the parity bar), 1e-3 for fp32.  The gather/dequantize kernel is
 bit-exact against the oracle's dequantization.
 """
 import numpy as np
