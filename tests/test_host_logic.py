@@ -205,3 +205,20 @@ def test_batched_cache_scale_granularity_arguments():
         BatchedPagedKVCache(1, 1, 4, 64, device="cpu", scale_granularity="token")
     with pytest.raises(ValueError):  # per-vector absmax is reduced over a power-of-two head_dim
         BatchedPagedKVCache(1, 1, 4, 96, device="cpu", scale_granularity="token_head")
+
+
+def test_bench_byte_counts_agree():
+    """The append sweep's byte count for any step size reduces to the decode
+    benchmark's one-token count, page commits included."""
+    import bench
+
+    for name in ("gpt2_int8", "tinyllama_int4"):
+        w = bench.WORKLOADS[name]
+        lens_after = [1, 15, 16, 17, 31, 32, 1024, 1009]
+        one = bench.append_bytes(lens_after, w)
+        many = bench.append_sweep_bytes([c - 1 for c in lens_after], lens_after, w)
+        assert one == many
+        # a 64-token step over one sequence: 4 page commits, no staged rows read or written
+        P, row = w["page"], w["hkv"] * w["d"]
+        bq = 1.0 if w["kv"] == "int8" else 0.5
+        assert bench.append_sweep_bytes([0], [64], w) == 2 * 64 * row * 2 + 4 * (2 * P * row * bq + 8)
