@@ -495,8 +495,10 @@ __device__ __forceinline__ void load_tile(TileRegs<KV4, HD>& T, MetaCache& mc, c
                 if ((lane & 15) == 0) prefetch_l2((lane < 16 ? p.k_scales : p.v_scales) + pa);
             }
         };
-        if (2 * jt + 1 < kPrefetchTiles) prefetch_tile(2 * jt + 1);
-        if (2 * jt + 2 < kPrefetchTiles) prefetch_tile(2 * jt + 2);
+        if (2 * jt + 1 < kPrefetchTiles) {  // one test per tile once the opening is over
+            prefetch_tile(2 * jt + 1);
+            if (2 * jt + 2 < kPrefetchTiles) prefetch_tile(2 * jt + 2);
+        }
         prefetch_tile(jt + kPrefetchTiles);
     } else {
         const int P = p.P;
@@ -869,6 +871,33 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
             }
         }
         for (int j = 0; j < sc.nitems; ++j) {
+            if constexpr (R == 2 && HPW == 1 && NW <= kWarpsDeep) {
+                // Run of page tiles: while the item one ahead (the next to issue) is
+                // still a page tile of this segment, the issuing walk is at this
+                // segment with ji == j + 1, so tile jt + 1 loads straight into the
+                // other slot and tile jt is consumed, with none of the walk's
+                // segment and item-kind tests.  The segment's last tile goes
+                // through the walk below (its successor lies in a later segment).
+                if (j >= sc.ntail && j + 1 < sc.nitems) {
+                    const int nloc = sc.ntile;
+                    int jt = j - sc.ntail;
+                    for (; jt + 1 < nloc; ++jt) {
+                        if (phase == 0) {
+                            load_tile<KV4, HD, P16>(tb[1], mc, p, si, jt + 1, nloc, hbase, wsub, WPH, g, c, lane);
+                            attend_tile<KV4, HD, NT, SPLIT, P16>(st[0], tb[0], p.sm_scale_log2);
+                        } else {
+                            load_tile<KV4, HD, P16>(tb[0], mc, p, si, jt + 1, nloc, hbase, wsub, WPH, g, c, lane);
+                            attend_tile<KV4, HD, NT, SPLIT, P16>(st[0], tb[1], p.sm_scale_log2);
+                        }
+                        phase ^= 1;
+                    }
+                    // the walk has issued every item of the segment; the next issue
+                    // goes into the slot after the one that holds the last tile
+                    ji = sc.nitems;
+                    iphase = phase ^ 1;
+                    j = sc.ntail + jt;
+                }
+            }
             issue();  // item k + R - 1 into the slot freed by item k - 1
             consume(phase, sc, j);
             phase = (phase + 1 == R) ? 0 : phase + 1;
