@@ -159,25 +159,29 @@ struct Cfg {
 };
 
 // BYTES (4, 8, 16 or 32, naturally aligned) of page data per lane into
-// 32-bit words: streaming loads (read once per launch, evict first).
+// 32-bit words, cached in L2 only (ld.global.cg).  Not evict-first: the rows of
+// neighbouring kv heads share 128-byte lines (one line prefetch serves them
+// all), and a line marked evict-first after the first head's read could leave
+// L2 before the other heads' warps, which drift apart over a long segment,
+// read their sectors -- measured as 31 % more DRAM bytes than the pages hold.
 template <int BYTES>
 __device__ __forceinline__ void ldg_words(const uint8_t* p, uint32_t (&w)[BYTES / 4]) {
     if constexpr (BYTES == 4) {
-        w[0] = __ldcs(reinterpret_cast<const unsigned int*>(p));
+        w[0] = __ldcg(reinterpret_cast<const unsigned int*>(p));
     } else if constexpr (BYTES == 8) {
-        const uint2 v = __ldcs(reinterpret_cast<const uint2*>(p));
+        const uint2 v = __ldcg(reinterpret_cast<const uint2*>(p));
         w[0] = v.x;
         w[1] = v.y;
     } else if constexpr (BYTES == 16) {
-        const uint4 v = __ldcs(reinterpret_cast<const uint4*>(p));
+        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(p));
         w[0] = v.x;
         w[1] = v.y;
         w[2] = v.z;
         w[3] = v.w;
     } else {
         static_assert(BYTES == 32, "row chunk");
-        const uint4 v = __ldcs(reinterpret_cast<const uint4*>(p));
-        const uint4 u = __ldcs(reinterpret_cast<const uint4*>(p + 16));
+        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(p));
+        const uint4 u = __ldcg(reinterpret_cast<const uint4*>(p + 16));
         w[0] = v.x;
         w[1] = v.y;
         w[2] = v.z;
