@@ -57,6 +57,7 @@ typedef enum mg_status {
 #define MG_DEV_SKIPPED 0x20          /* a kernel skipped its work because an earlier bit was set */
 #define MG_DEV_CONTEXT_OVERFLOW 0x40 /* reserved (no current kernel sets it) */
 #define MG_DEV_BAD_ARGUMENT 0x80     /* a per-sequence argument (n_new > max_new, seq id, cu_seqlens) was inconsistent; that sequence was skipped */
+#define MG_DEV_BAD_LENGTH 0x100      /* mg_plan_append: a negative n_new or seq_lens entry; the step changed nothing */
 
 typedef enum mg_kv_dtype { MG_KV_INT8 = 0, MG_KV_INT4 = 1 } mg_kv_dtype;
 /* Scale granularity of a batched pool.  MG_SCALE_PAGE is the reference's only
@@ -184,8 +185,9 @@ MG_API mg_status mg_alloc_init(const mg_allocator* alloc, mg_stream_t stream);
  * order and pages in logical order (so the ids equal a reference
  * BlockAllocator replaying the same commits) and written to
  * block_tables[b, j].  All-or-nothing: when the commits exceed the free pages
- * (MG_DEV_OUT_OF_PAGES) or a row (MG_DEV_BLOCK_TABLE_FULL), nothing changes and
- * the append/attention calls that take the same dev_status skip their work. */
+ * (MG_DEV_OUT_OF_PAGES) or a row (MG_DEV_BLOCK_TABLE_FULL), or a length or
+ * count is negative (MG_DEV_BAD_LENGTH), nothing changes and the
+ * append/attention calls that take the same dev_status skip their work. */
 MG_API mg_status mg_plan_append(const mg_allocator* alloc, int32_t* block_tables, int32_t max_blocks,
                          int32_t* seq_lens, const int32_t* n_new, int32_t batch, int32_t page_size,
                          int32_t* dev_status, mg_stream_t stream);
@@ -196,7 +198,9 @@ MG_API mg_status mg_plan_append(const mg_allocator* alloc, int32_t* block_tables
  * one fresh absmax scale over the whole page (K and V separately) exactly as
  * metagross/cache.py:63-72 + csrc/quantize.cu; with MG_SCALE_TOKEN_HEAD every
  * (token, head) D-vector of the page gets its own fresh absmax scale.  The
- * partial page's tokens go to staging unquantized. */
+ * partial page's tokens go to staging unquantized.  One call writes at most
+ * 65534 pages per sequence (max_new <= 65534 * page_size); a longer prefill
+ * is split over several steps. */
 MG_API mg_status mg_kv_append(const mg_cache_layout* layout, const mg_layer_ptrs* layer,
                        const int32_t* block_tables, const int32_t* seq_lens, const int32_t* n_new,
                        int32_t batch, const void* k_new, const void* v_new, int32_t new_dtype,

@@ -47,6 +47,7 @@ MG_DEV_BITS = {
     0x20: "work skipped after an earlier error",
     0x40: "sequence longer than max_context",
     0x80: "inconsistent per-sequence argument",
+    0x100: "negative length or token count",
 }
 
 

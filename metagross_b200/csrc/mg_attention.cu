@@ -210,8 +210,12 @@ extern "C" int64_t mg_paged_decode_workspace_bytes(const mg_cache_layout* L, int
     if (!L) return 0;
     DecodePlan pl;
     (void)max_context;
-    if (make_decode_plan(L->kv_dtype == MG_KV_INT4, L->head_dim, L->page_size, L->num_kv_heads, num_q_heads, 0, batch,
-                         L->staging_dtype == MG_F16 ? 2 : 4, &pl) != MG_OK)
+    // The size does not depend on the query dtype, but the set of supported
+    // shapes does (GQA groups of 9-16 run with fp16 queries only): size from
+    // whichever plan exists, fp32 queries first.
+    const int kv4 = L->kv_dtype == MG_KV_INT4, esz = L->staging_dtype == MG_F16 ? 2 : 4;
+    if (make_decode_plan(kv4, L->head_dim, L->page_size, L->num_kv_heads, num_q_heads, 0, batch, esz, &pl) != MG_OK &&
+        make_decode_plan(kv4, L->head_dim, L->page_size, L->num_kv_heads, num_q_heads, 1, batch, esz, &pl) != MG_OK)
         return 0;
     return pl.ws_bytes;  // independent of the query dtype and of max_context
 }

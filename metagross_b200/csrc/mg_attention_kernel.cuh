@@ -691,7 +691,7 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
         const int32_t h0 = __ldcg(p.plan), h1 = __ldcg(p.plan + 1), h2 = __ldcg(p.plan + 2), h4 = __ldcg(p.plan + 4);
         const int32_t h8 = __ldcg(p.plan + 8);
         const int32_t cnt = __ldcg(p.plan + p.lay.off_counts + cta), off = __ldcg(p.plan + p.lay.off_offs + cta);
-        const bool stop = (stat & (MG_DEV_OUT_OF_PAGES | MG_DEV_BLOCK_TABLE_FULL)) != 0;
+        const bool stop = (stat & (MG_DEV_OUT_OF_PAGES | MG_DEV_BLOCK_TABLE_FULL | MG_DEV_BAD_LENGTH)) != 0;
         const bool ok = h0 == kPlanMagic && h1 == p.batch && h2 == static_cast<int>(gridDim.x) && h8 == p.has_staging;
         if (!ok && !stop) flag(p.status, MG_DEV_BAD_ARGUMENT);
         sm_hdr[0] = (ok && !stop) ? cnt : 0;

@@ -26,7 +26,7 @@ __global__ void alloc_init_kernel(int32_t* free_stack, int32_t* n_free, int32_t*
     if (blockIdx.x == 0 && threadIdx.x == 0) *n_free = static_cast<int32_t>(n);
 }
 
-constexpr int32_t kStopBits = MG_DEV_OUT_OF_PAGES | MG_DEV_BLOCK_TABLE_FULL;
+constexpr int32_t kStopBits = MG_DEV_OUT_OF_PAGES | MG_DEV_BLOCK_TABLE_FULL | MG_DEV_BAD_LENGTH;
 
 // One CTA.  Pass 1 validates the whole step, pass 2 applies it, so a failed
 // step changes nothing.
@@ -44,21 +44,22 @@ __global__ void __launch_bounds__(kPlanThreads) plan_append_kernel(int32_t* free
         return;
     }
     int local = 0;
-    int bad = 0;
+    int bad = 0;  // bit 0: a row would overflow; bit 1: a negative length or count
     for (int b = threadIdx.x; b < batch; b += blockDim.x) {
         const int old = seq_lens[b], add = n_new[b];
-        if (add < 0 || old < 0) { bad = 1; continue; }
+        if (add < 0 || old < 0) { bad |= 2; continue; }
         const int nw = old + add;
-        if (nw / P > max_blocks) bad = 1;
+        if (nw / P > max_blocks) bad |= 1;
         local += nw / P - old / P;
     }
     int total;
-    if (bad) atomicOr(&s_flags, 1);
+    if (bad) atomicOr(&s_flags, bad);
     (void)block_exclusive_scan(local, scratch, &total);
     __syncthreads();
     const int n_free = *n_free_p;
     if (s_flags) {
-        if (threadIdx.x == 0) flag(status, MG_DEV_BLOCK_TABLE_FULL);
+        if (threadIdx.x == 0)
+            flag(status, ((s_flags & 1) ? MG_DEV_BLOCK_TABLE_FULL : 0) | ((s_flags & 2) ? MG_DEV_BAD_LENGTH : 0));
         return;
     }
     if (total > n_free) {
@@ -638,8 +639,12 @@ extern "C" mg_status mg_kv_append(const mg_cache_layout* L, const mg_layer_ptrs*
     p.scale_th = L->scale_layout == MG_SCALE_TOKEN_HEAD;
     p.num_pages = L->num_pages;
     p.status = dev_status;
-    const int touch = (max_new + L->page_size - 1) / L->page_size + 1;
-    dim3 grid(batch, touch, 2);
+    const int64_t touch = (static_cast<int64_t>(max_new) + L->page_size - 1) / L->page_size + 1;
+    MG_REQUIRE(touch <= 65535,
+               "max_new %d spans %lld pages of %d tokens; one append takes at most 65534 pages per sequence "
+               "(split the prefill into several steps)",
+               max_new, (long long)touch - 1, L->page_size);
+    dim3 grid(batch, static_cast<unsigned>(touch), 2);
     const bool i4 = L->kv_dtype == MG_KV_INT4;
     const bool s16 = L->staging_dtype == MG_F16, n16 = new_dtype == MG_F16;
     cudaStream_t s = as_stream(stream);

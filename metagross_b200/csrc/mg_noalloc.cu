@@ -16,6 +16,7 @@
 // array keeps whatever the previous call left) and then runs
 // mg_paged_decode_attention on the array.  Calls that overlap on the GPU
 // share the array and race: run one at a time per device.
+#include <cstdio>
 #include <mutex>
 
 #include "mg_common.cuh"
@@ -62,7 +63,13 @@ extern "C" mg_status mg_paged_decode_attention_noalloc(const mg_cache_layout* L,
     MG_REQUIRE(batch >= 0, "batch must be >= 0");
     if (batch == 0) return MG_OK;
     const int64_t need = mg_paged_decode_workspace_bytes(L, batch, num_q_heads, max_context);
-    if (need <= 0) return set_error(MG_ERR_INVALID_ARGUMENT, "%s", mg_last_error());
+    if (need <= 0) {
+        // the sizing call left its reason in the thread's error text: copy it
+        // out before formatting into that same buffer
+        char why[512];
+        snprintf(why, sizeof(why), "%s", mg_last_error());
+        return set_error(MG_ERR_INVALID_ARGUMENT, "no-alloc decode attention: %s", why);
+    }
     MG_REQUIRE(need <= kNoAllocScratchBytes,
                "no-alloc decode attention needs %lld bytes of workspace, more than its %lld-byte static scratch "
                "(smaller batch or fewer heads, or use mg_paged_decode_attention with a caller workspace)",

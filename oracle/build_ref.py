@@ -12,7 +12,8 @@ recipe, not the reference's ``setup.py``.  The module is named
 It targets sm_100 (the arch the reference's own build would pick for
 ``TORCH_CUDA_ARCH_LIST=10.0``).
 
-Run here (where the reference sources are mounted):
+Run where the reference sources are mounted (the path argument, else
+``$METAGROSS_REFERENCE_ROOT``, else the default mount point below):
     python oracle/build_ref.py [/path/to/reference]
 The output ``oracle/_ref/metagross_ref_C*.so`` is git-ignored but travels to
 the GPU box with the working tree.
@@ -38,14 +39,29 @@ REF_SOURCES = [
 ]
 
 
+# Where the reference's sources are read from: the environment variable
+# METAGROSS_REFERENCE_ROOT, else the recipe's default mount point.
+DEFAULT_REFERENCE_ROOT = "/root/reference"
+
+
+def reference_root() -> str:
+    return os.environ.get("METAGROSS_REFERENCE_ROOT", DEFAULT_REFERENCE_ROOT)
+
+
+def sources_present(root: str | None = None) -> bool:
+    root = root or reference_root()
+    return all(os.path.exists(os.path.join(root, s)) for s in REF_SOURCES)
+
+
 def built_module_path() -> str | None:
     hits = sorted(glob.glob(os.path.join(OUT_DIR, "metagross_ref_C*.so")))
     return hits[0] if hits else None
 
 
-def build(reference_root: str = "/root/reference", verbose: bool = False) -> str | None:
+def build(root: str | None = None, verbose: bool = False) -> str | None:
     """Compile the reference ``_C`` if its sources are present; return the .so path."""
-    srcs = [os.path.join(reference_root, s) for s in REF_SOURCES]
+    root = root or reference_root()
+    srcs = [os.path.join(root, s) for s in REF_SOURCES]
     if not all(os.path.exists(s) for s in srcs):
         return built_module_path()
     newest_src = max(os.path.getmtime(s) for s in srcs)
@@ -58,7 +74,7 @@ def build(reference_root: str = "/root/reference", verbose: bool = False) -> str
     load(
         name="metagross_ref_C",
         sources=srcs,
-        extra_include_paths=[os.path.join(reference_root, "csrc")],
+        extra_include_paths=[os.path.join(root, "csrc")],
         extra_cuda_cflags=["-O3", "-gencode=arch=compute_100,code=sm_100"],
         extra_cflags=["-O3"],
         build_directory=BUILD_DIR,
@@ -74,5 +90,4 @@ def build(reference_root: str = "/root/reference", verbose: bool = False) -> str
 
 
 if __name__ == "__main__":
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
-    print(build(root, verbose=True))
+    print(build(sys.argv[1] if len(sys.argv) > 1 else None, verbose=True))

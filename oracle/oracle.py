@@ -345,10 +345,23 @@ class PagedCacheModel:
         if n_new is None:
             n_new = [T] * B
         for b in range(B):
-            for i in range(int(n_new[b])):
+            n = int(n_new[b])
+            i = 0
+            while i < n:
+                r = len(self.staging_k[b])
+                if r == 0 and n - i >= self.P:
+                    # a whole page with nothing staged: the same commit as pushing
+                    # its P tokens one by one (metagross/cache.py:57-61), in one go
+                    self.staging_k[b] = list(k_new[b, i:i + self.P].astype(self.staging_dtype))
+                    self.staging_v[b] = list(v_new[b, i:i + self.P].astype(self.staging_dtype))
+                    self.seq_lens[b] += self.P
+                    i += self.P
+                    self._commit(b)
+                    continue
                 self.staging_k[b].append(k_new[b, i].astype(self.staging_dtype))
                 self.staging_v[b].append(v_new[b, i].astype(self.staging_dtype))
                 self.seq_lens[b] += 1
+                i += 1
                 if len(self.staging_k[b]) == self.P:
                     self._commit(b)
 

@@ -94,3 +94,49 @@ def test_extension_rejects_cpu_tensors(op):
             _C.quantize_new_scale(x, page, 0)
         else:
             _C.dequantize_page(page, 0, 4, 0.1)
+
+
+class _Layout(ctypes.Structure):
+    _fields_ = [("kv_dtype", ctypes.c_int32), ("staging_dtype", ctypes.c_int32), ("page_size", ctypes.c_int32),
+                ("num_kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("max_blocks", ctypes.c_int32),
+                ("num_pages", ctypes.c_int64), ("scale_layout", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+
+
+@pytest.mark.parametrize("hq,hkv", [(32, 2), (16, 1), (8, 1), (12, 12)])
+def test_workspace_size_covers_every_supported_group(hq, hkv):
+    """Groups of 9-16 q heads per kv head run with fp16 queries only; the
+    workspace size (independent of the query dtype) must still be given."""
+    lib = ctypes.CDLL(LIB)
+    lib.mg_paged_decode_workspace_bytes.restype = ctypes.c_int64
+    lib.mg_last_error.restype = ctypes.c_char_p
+    L = _Layout(1, 1, 16, hkv, 64, 64, 4096)
+    n = lib.mg_paged_decode_workspace_bytes(ctypes.byref(L), 8, hq, 1024)
+    assert n > 0, lib.mg_last_error()
+
+
+def test_workspace_size_rejects_an_unsupported_group():
+    lib = ctypes.CDLL(LIB)
+    lib.mg_paged_decode_workspace_bytes.restype = ctypes.c_int64
+    lib.mg_last_error.restype = ctypes.c_char_p
+    L = _Layout(0, 1, 16, 1, 64, 64, 4096)
+    assert lib.mg_paged_decode_workspace_bytes(ctypes.byref(L), 8, 17, 1024) == 0
+    assert b"GQA group 17" in lib.mg_last_error()
+
+
+def test_append_rejects_more_pages_than_one_launch_covers():
+    lib = ctypes.CDLL(LIB)
+    lib.mg_last_error.restype = ctypes.c_char_p
+
+    class _Ptrs(ctypes.Structure):
+        _fields_ = [(n, ctypes.c_void_p) for n in ("k_pool", "v_pool", "k_scales", "v_scales", "staging_k",
+                                                    "staging_v")]
+
+    L = _Layout(0, 1, 16, 4, 64, 70000, 1 << 20)
+    ptrs = _Ptrs(*([1 << 20] * 6))  # never dereferenced: refused before launch
+    f = lib.mg_kv_append
+    f.restype = ctypes.c_int
+    rc = f(ctypes.byref(L), ctypes.byref(ptrs), ctypes.c_void_p(1 << 20), ctypes.c_void_p(1 << 20),
+           ctypes.c_void_p(1 << 20), 1, ctypes.c_void_p(1 << 20), ctypes.c_void_p(1 << 20), 1, 16 * 65535,
+           None, None)
+    assert rc == 1
+    assert b"65534 pages" in lib.mg_last_error()

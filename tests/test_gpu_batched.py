@@ -92,7 +92,7 @@ def test_decode_attention_matches_oracle_fp16_int8_mha():
 
 
 @pytest.mark.parametrize("kv", ["int8", "int4"])
-@pytest.mark.parametrize("hq,hkv", [(32, 4), (8, 8), (12, 4), (16, 2)])
+@pytest.mark.parametrize("hq,hkv", [(32, 4), (8, 8), (12, 4), (16, 2), (32, 2)])
 @pytest.mark.parametrize("qdt", [torch.float16, torch.float32])
 def test_decode_attention_gqa(kv, hq, hkv, qdt):
     if qdt == torch.float32 and hq // hkv > 8:
@@ -216,6 +216,22 @@ def test_out_of_pages_is_all_or_nothing():
     assert cache.seq_lens.tolist() == [0, 0]
     assert cache.allocator.num_free == 3
     with pytest.raises(RuntimeError, match="out of pages"):
+        cache.check()
+
+
+def test_negative_count_is_rejected_and_changes_nothing():
+    B, H, D, P = 3, 2, 64, 16
+    cache = _cache_cls()(1, B, H, D, page_size=P, num_pages=8, max_blocks=4)
+    k = torch.randn(B, 20, H, D).half().cuda()
+    cache.begin_step(torch.tensor([20, -1, 5], dtype=torch.int32))
+    cache.append(0, k, k)
+    q = torch.randn(B, H, D).half().cuda()
+    cache.attend(0, q)
+    assert cache.seq_lens.tolist() == [0, 0, 0]
+    assert cache.allocator.num_free == 8
+    s = int(cache.status.item())
+    assert s & 0x100 and not s & 0x10, hex(s)  # the cause is named, not reported as a full block-table row
+    with pytest.raises(RuntimeError, match="negative length"):
         cache.check()
 
 

@@ -63,7 +63,7 @@ def _args(cache):
     return L, ptrs
 
 
-@pytest.mark.parametrize("kv,B,hkv,hq", [("int8", 6, 12, 12), ("int4", 9, 4, 32)])
+@pytest.mark.parametrize("kv,B,hkv,hq", [("int8", 6, 12, 12), ("int4", 9, 4, 32), ("int4", 5, 2, 32)])
 def test_noalloc_matches_workspace_entry_point(kv, B, hkv, hq):
     lib = _lib()
     cache, q = _filled_cache(kv, B, hkv, hq, seed=11 + B)
