@@ -481,6 +481,279 @@ def decode_model(device, batch=64, prompt_len=128, new_tokens=256, kv="int8"):
             "first_tokens": toks[0, :8].tolist()}
 
 
+def reference_cuda_leg(cache, w, q, sample_steps=3):
+    """The reference's own CUDA path on the same cache, as its wrapper drives it
+    (metagross/attention.py:104-134 over csrc/paged_attention.cu:139-255 and
+    csrc/quantize.cu:65-120): one ``paged_attention_committed`` call per
+    sequence per layer (fp32 q, the sequence's committed pages through its
+    block table) and one ``quantize_new_scale`` per committed page for K and
+    for V.  The module is the unmodified reference built for sm_100 by its own
+    setup.py into baseline/_ref.  Every layer pool is visited in turn (12 x
+    50 MB > L2).  The staged tail, which the reference wrapper attends in torch,
+    is not timed (so the comparison favours the reference)."""
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "metagross")):
+        return {"unavailable": "reference not installed in baseline/_ref"}
+    if w["kv"] != "int8" or w["d"] != 64:
+        return {"unavailable": "the reference's committed-page attention is INT8 with head_dim 64 only"}
+    sys.path.insert(0, ref_dir)
+    try:
+        from metagross import _C as ref_C
+    finally:
+        sys.path.remove(ref_dir)
+    L, B, P = cache.num_layers, cache.batch, cache.page_size
+    lens = cache.seq_lens.cpu().tolist()
+    tables = [cache.block_tables[b, : lens[b] // P].contiguous() for b in range(B)]
+    qf = q.float()
+    scale = 1.0 / math.sqrt(w["d"])
+
+    def one_step():
+        for layer in range(L):
+            for b in range(B):
+                ref_C.paged_attention_committed(qf[layer, b], cache.k_pool[layer], cache.v_pool[layer],
+                                                cache.k_scales[layer], cache.v_scales[layer], tables[b], scale)
+
+    one_step()  # warm-up
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record()
+    for _ in range(sample_steps):
+        one_step()
+    e1.record()
+    torch.cuda.synchronize()
+    wall_ms = (time.perf_counter() - t0) * 1e3 / sample_steps
+    att_ms = e0.elapsed_time(e1) / sample_steps
+    # a page commit: quantize_new_scale on a [P, Hkv, D] fp32 page, K and V
+    g = torch.Generator(device=q.device).manual_seed(7)
+    src = torch.randn(P, w["hkv"], w["d"], generator=g, device=q.device)
+    dst = torch.zeros(P, w["hkv"], w["d"], dtype=torch.int8, device=q.device)
+    for _ in range(5):
+        ref_C.quantize_new_scale(src, dst, 0)
+    torch.cuda.synchronize()
+    nq = 64
+    e0.record()
+    for _ in range(nq):
+        ref_C.quantize_new_scale(src, dst, 0)
+    e1.record()
+    torch.cuda.synchronize()
+    q_ms = e0.elapsed_time(e1) / nq
+    # one decode step commits a page for every sequence every P steps, in every layer, K and V
+    step_ms = att_ms + L * B * 2 * q_ms / P
+    committed = [(c // P) * P for c in lens]
+    att_bytes = L * attention_bytes(committed, w)
+    return {"kind": "ref_C_sm100", "module": "metagross._C of the unmodified reference, built for sm_100 by its "
+                                              "setup.py into baseline/_ref",
+            "ms_per_step": round(step_ms, 4), "attention_ms_per_step": round(att_ms, 4),
+            "attention_wall_ms_per_step": round(wall_ms, 4), "quantize_ms_per_call": round(q_ms, 5),
+            "attention_calls_per_step": L * B, "attention_gbs": round(att_bytes / (att_ms / 1e3) / 1e9, 1),
+            "unit": "GB/s",
+            "note": f"{sample_steps} steps x {L} layers x {B} calls (one per sequence, fp32 q, committed pages); "
+                    f"quantize_new_scale per committed page (K and V), every {P} steps per sequence; the staged "
+                    f"tail (torch in the reference wrapper) not timed"}
+
+
+def measure(w, name, steps, warmup, world, rank, local, device, e2e=True, equal_counts=True, min_timed_s=1.0):
+    """Build the workload on this rank and time it.  Returns a dict of the
+    figures (rank-0 aggregates already reduced over ranks)."""
+    sharded = bool(w.get("sharded", False))
+    gatherer = None
+    gather_buf = None
+    loads = None
+    if sharded:
+        # one global batch, split over the ranks by context length (strong scaling)
+        from metagross_b200.sharding import ShardGather, lpt_shard, shard_loads
+
+        glob_ctx = contexts_for(w, w["batch"], seed=1234)
+        shards = lpt_shard(glob_ctx.numpy(), world, equal_counts=equal_counts)
+        loads = shard_loads(glob_ctx.numpy(), shards)
+        cache, sched, max_ctx, q, kn, vn, out = build(w, device, seed=1234 + rank,
+                                                      ctx=glob_ctx[torch.as_tensor(shards[rank])])
+        if world > 1:
+            gatherer = ShardGather(shards, rank, (w["hq"], w["d"]), torch.float16, device)
+    else:
+        # every rank runs the same per-GPU workload on its own sequences (weak scaling)
+        cache, sched, max_ctx, q, kn, vn, out = build(w, device, seed=1234 + rank)
+        if world > 1:
+            gather_buf = torch.empty(world * w["batch"], w["hq"], w["d"], device=device, dtype=torch.float16)
+    L, B = w["layers"], cache.batch
+    e2e_steps = max(3, steps // 2)
+    warm_plans = plan_steps(sched, warmup, device)
+
+    from metagross_b200 import DecodeGraph
+
+    def gather():
+        if world > 1:
+            import torch.distributed as dist
+
+            if gatherer is not None:
+                # every rank's last-layer outputs on every rank: the padded rank-major buffer
+                # and the per-rank lengths (the global order is one index_select away)
+                gatherer(out[L - 1], reorder=False)
+            else:
+                dist.all_gather_into_tensor(gather_buf, out[L - 1])
+
+    for pl in warm_plans[:2]:  # eager steps (allocate the workspace and plan buffers)
+        run_step(cache, q, kn, vn, out, pl, max_ctx)
+        gather()
+    graph = DecodeGraph(cache, q, kn, vn, out, n_new=1)
+
+    def step(plan):
+        ids, lens, _ = plan
+        if ids is not None:
+            cache.truncate(lens, ids)
+        graph.replay()
+        gather()
+
+    t_w0 = time.perf_counter()
+    for pl in warm_plans[2:]:
+        step(pl)
+    torch.cuda.synchronize()
+    cache.check()
+    # repeats of the K timed steps, so that the clock sampler sees >= min_timed_s of load
+    est = (time.perf_counter() - t_w0) / max(1, len(warm_plans) - 2)
+    repeats = int(min(200, max(1, math.ceil(min_timed_s / max(steps * est, 1e-6)))))
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([repeats], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        repeats = int(t.item())
+    timed_plans = [plan_steps(sched, steps, device) for _ in range(repeats)]
+    e2e_plans = plan_steps(sched, e2e_steps, device)
+
+    # bytes of the timed steps (lengths known on the host)
+    att_b, app_b = 0.0, 0.0
+    n_trunc = 0
+    for rp in timed_plans:
+        for ids, _, after in rp:
+            att_b += L * attention_bytes(after, w)
+            app_b += L * append_bytes(after, w)
+            n_trunc += ids is not None
+    step_bytes = (att_b + app_b) / (steps * repeats)
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    clocks.mark_start()
+    ms_rep = []
+    for r in range(repeats):
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for s_ in range(steps):
+            step(timed_plans[r][s_])
+        t1.record()
+        torch.cuda.synchronize()
+        ms_rep.append(t0.elapsed_time(t1))
+    clocks.mark_stop()
+    clk = clocks.stop()
+    ms = float(sum(ms_rep)) / repeats  # K steps
+    cache.check()
+
+    # ---- the attention kernel alone: a graph of the L attention launches ------------
+    cache._decode_plan()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    g_att = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(g_att, stream=side):
+            for layer in range(L):
+                cache.attend(layer, q[layer], out=out[layer], max_context=max_ctx)
+    torch.cuda.current_stream().wait_stream(side)
+    for _ in range(3):
+        g_att.replay()
+    att_reps = max(5, min(50, steps // 4))
+    a0 = torch.cuda.Event(enable_timing=True)
+    a1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a0.record()
+    for _ in range(att_reps):
+        g_att.replay()
+    a1.record()
+    torch.cuda.synchronize()
+    att_avg_ms = a0.elapsed_time(a1) / (att_reps * L)
+    att_lens = timed_plans[-1][-1][2]
+    att_bytes_per_launch = attention_bytes(att_lens, w)
+    del g_att
+    gather_ms = 0.0
+    if world > 1:
+        import torch.distributed as dist
+
+        # the per-step output gather alone (NCCL over NVLink), reported beside the step
+        dist.barrier()
+        torch.cuda.synchronize()
+        g0 = torch.cuda.Event(enable_timing=True)
+        g1 = torch.cuda.Event(enable_timing=True)
+        g0.record()
+        for _ in range(20):
+            gather()
+        g1.record()
+        torch.cuda.synchronize()
+        gather_ms = g0.elapsed_time(g1) / 20
+        t = torch.tensor([ms, att_avg_ms, gather_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, att_avg_ms, gather_ms = float(t[0]), float(t[1]), float(t[2])
+
+    res = {"ms": ms, "steps": steps, "repeats": repeats, "ms_per_repeat": [round(x, 3) for x in ms_rep],
+           "att_avg_ms": att_avg_ms, "att_bytes_per_launch": att_bytes_per_launch, "gather_ms": gather_ms,
+           "clk": clk, "n_trunc": n_trunc, "L": L, "sharded": sharded, "loads": loads,
+           "att_reps": att_reps, "cache": cache, "q": q}
+
+    # ---- end to end through the public API with host buffers -----------------
+    e_bytes = 0.0
+    e_ms = None
+    if e2e:
+        qh = q.cpu().pin_memory()
+        knh, vnh = kn.cpu().pin_memory(), vn.cpu().pin_memory()
+        outh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        for _, _, after in e2e_plans:
+            e_bytes += L * (attention_bytes(after, w) + append_bytes(after, w))
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for s_ in range(e2e_steps):
+            q.copy_(qh, non_blocking=True)  # the graph's input buffers, refilled from pinned host memory
+            kn.copy_(knh, non_blocking=True)
+            vn.copy_(vnh, non_blocking=True)
+            step(e2e_plans[s_])
+            outh.copy_(out, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        e_ms = e0.elapsed_time(e1)
+        if world > 1:
+            import torch.distributed as dist
+
+            t = torch.tensor([e_ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = float(t[0])
+        res["e2e_io"] = (int(q.numel() * 2 + kn.numel() * 2 + vn.numel() * 2), int(out.numel() * 2))
+    # whole-job totals: every rank's own bytes and sequences, summed
+    tot_step_bytes, tot_e_bytes, tot_batch = step_bytes, e_bytes, float(B)
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([step_bytes, e_bytes, float(B)], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        tot_step_bytes, tot_e_bytes, tot_batch = float(t[0]), float(t[1]), float(t[2])
+    cache.check()
+    res.update(tot_step_bytes=tot_step_bytes, tot_e_bytes=tot_e_bytes, tot_batch=tot_batch, e_ms=e_ms,
+               e2e_steps=e2e_steps,
+               ctx_mean=float(np.mean([np.mean(a) for rp in timed_plans for _, _, a in rp])),
+               value=tot_step_bytes / (ms / steps / 1e3) / 1e9)
+    graph = None
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -490,6 +763,13 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="gpt2_int8")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-cuda", action="store_true",
+                    help="skip timing the reference's own CUDA ops (baseline/_ref) beside the line")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the 1024-sequence log-normal INT4 strong-scaling figures that ride along with the "
+                         "default workload")
+    ap.add_argument("--min-timed-s", type=float, default=1.0,
+                    help="repeat the K timed steps until the timed region lasts this long (clock sampling)")
     ap.add_argument("--layers", type=int, default=None,
                     help="override the workload's layer count (a small case for profiling; the default run uses "
                          "the workload's own depth)")
@@ -550,209 +830,85 @@ def main():
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
 
-    sharded = bool(w.get("sharded", False))
-    gatherer = None
-    gather_buf = None
-    if sharded:
-        # one global batch, split over the ranks by context length (strong scaling)
-        from metagross_b200.sharding import ShardGather, lpt_shard
+    m = measure(w, args.workload, args.steps, args.warmup, world, rank, local, device,
+                min_timed_s=args.min_timed_s)
+    ref_cuda = None
+    if world == 1 and rank == 0 and not args.no_reference_cuda and args.workload == "gpt2_int8":
+        ref_cuda = reference_cuda_leg(m["cache"], w, m["q"])
+    m["cache"] = m["q"] = None
+    torch.cuda.empty_cache()
 
-        glob_ctx = contexts_for(w, w["batch"], seed=1234)
-        shards = lpt_shard(glob_ctx.numpy(), world, equal_counts=True)
-        cache, sched, max_ctx, q, kn, vn, out = build(w, device, seed=1234 + rank,
-                                                      ctx=glob_ctx[torch.as_tensor(shards[rank])])
-        if world > 1:
-            gatherer = ShardGather(shards, rank, (w["hq"], w["d"]), torch.float16, device)
-    else:
-        # every rank runs the same per-GPU workload on its own sequences (weak scaling)
-        cache, sched, max_ctx, q, kn, vn, out = build(w, device, seed=1234 + rank)
-        if world > 1:
-            gather_buf = torch.empty(world * w["batch"], w["hq"], w["d"], device=device, dtype=torch.float16)
-    L, B = w["layers"], cache.batch
-    e2e_steps = max(3, args.steps // 2)
-    warm_plans = plan_steps(sched, args.warmup, device)
-    timed_plans = plan_steps(sched, args.steps, device)
-    e2e_plans = plan_steps(sched, e2e_steps, device)
-
-    from metagross_b200 import DecodeGraph
-
-    def gather():
-        if world > 1:
-            import torch.distributed as dist
-
-            if gatherer is not None:
-                # every rank's last-layer outputs on every rank: the padded rank-major buffer
-                # and the per-rank lengths (the global order is one index_select away)
-                gatherer(out[L - 1], reorder=False)
-            else:
-                dist.all_gather_into_tensor(gather_buf, out[L - 1])
-
-    for pl in warm_plans[:2]:  # eager steps (allocate the workspace and plan buffers)
-        run_step(cache, q, kn, vn, out, pl, max_ctx)
-        gather()
-    graph = DecodeGraph(cache, q, kn, vn, out, n_new=1)
-
-    def step(plan):
-        ids, lens, _ = plan
-        if ids is not None:
-            cache.truncate(lens, ids)
-        graph.replay()
-        gather()
-
-    for pl in warm_plans[2:]:
-        step(pl)
-    torch.cuda.synchronize()
-    cache.check()
-
-    # bytes of the timed steps (lengths known on the host)
-    att_b, app_b = 0.0, 0.0
-    n_trunc = 0
-    for ids, _, after in timed_plans:
-        att_b += L * attention_bytes(after, w)
-        app_b += L * append_bytes(after, w)
-        n_trunc += ids is not None
-    step_bytes = (att_b + app_b) / args.steps
-    att_bytes_per_launch = att_b / (args.steps * L)
-
-    clocks = ClockSampler(local)
-    clocks.start()
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier()
-    torch.cuda.synchronize()
-    clocks.mark_start()
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for s in range(args.steps):
-        step(timed_plans[s])
-    t1.record()
-    torch.cuda.synchronize()
-    clocks.mark_stop()
-    clk = clocks.stop()
-    ms = t0.elapsed_time(t1)
-    cache.check()
-
-    # ---- the attention kernel alone: a graph of the L attention launches ------------
-    cache._decode_plan()
-    side = torch.cuda.Stream()
-    side.wait_stream(torch.cuda.current_stream())
-    g_att = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(side):
-        with torch.cuda.graph(g_att, stream=side):
-            for layer in range(L):
-                cache.attend(layer, q[layer], out=out[layer], max_context=max_ctx)
-    torch.cuda.current_stream().wait_stream(side)
-    for _ in range(3):
-        g_att.replay()
-    att_reps = max(5, min(50, args.steps // 4))
-    a0 = torch.cuda.Event(enable_timing=True)
-    a1 = torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    a0.record()
-    for _ in range(att_reps):
-        g_att.replay()
-    a1.record()
-    torch.cuda.synchronize()
-    att_avg_ms = a0.elapsed_time(a1) / (att_reps * L)
-    att_lens = timed_plans[-1][2]
-    att_bytes_per_launch = attention_bytes(att_lens, w)
-    del g_att
-    gather_ms = 0.0
-    if world > 1:
-        import torch.distributed as dist
-
-        # the per-step output gather alone (NCCL over NVLink), reported beside the step
-        dist.barrier()
-        torch.cuda.synchronize()
-        g0 = torch.cuda.Event(enable_timing=True)
-        g1 = torch.cuda.Event(enable_timing=True)
-        g0.record()
-        for _ in range(20):
-            gather()
-        g1.record()
-        torch.cuda.synchronize()
-        gather_ms = g0.elapsed_time(g1) / 20
-        t = torch.tensor([ms, att_avg_ms, gather_ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, att_avg_ms, gather_ms = float(t[0]), float(t[1]), float(t[2])
-
-    # ---- end to end through the public API with host buffers -----------------
-    qh = q.cpu().pin_memory()
-    knh, vnh = kn.cpu().pin_memory(), vn.cpu().pin_memory()
-    outh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    e_bytes = 0.0
-    for _, _, after in e2e_plans:
-        e_bytes += L * (attention_bytes(after, w) + append_bytes(after, w))
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for s in range(e2e_steps):
-        q.copy_(qh, non_blocking=True)  # the graph's input buffers, refilled from pinned host memory
-        kn.copy_(knh, non_blocking=True)
-        vn.copy_(vnh, non_blocking=True)
-        step(e2e_plans[s])
-        outh.copy_(out, non_blocking=True)
-    e1.record()
-    torch.cuda.synchronize()
-    e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        import torch.distributed as dist
-
-        t = torch.tensor([e_ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e_ms = float(t[0])
-    # whole-job totals: every rank's own bytes and sequences, summed
-    tot_step_bytes, tot_e_bytes, tot_batch = step_bytes, e_bytes, float(B)
-    if world > 1:
-        import torch.distributed as dist
-
-        t = torch.tensor([step_bytes, e_bytes, float(B)], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        tot_step_bytes, tot_e_bytes, tot_batch = float(t[0]), float(t[1]), float(t[2])
-    e2e = {"value": round(tot_e_bytes / (e_ms / 1e3) / 1e9, 1), "unit": "GB/s",
-           "h2d_bytes_per_step": int(q.numel() * 2 + kn.numel() * 2 + vn.numel() * 2),
-           "d2h_bytes_per_step": int(out.numel() * 2), "ms_per_step": e_ms / e2e_steps}
-    cache.check()
-    ctx_mean = float(np.mean([np.mean(a) for _, _, a in timed_plans]))
+    # the 1024-sequence log-normal INT4 configuration, split over the ranks by
+    # total tokens (strong scaling), beside the default workload at every N
+    sharded_fig = None
+    if not args.no_sharded and args.workload == "gpt2_int8" and args.layers is None:
+        ws = dict(WORKLOADS["lognormal_int4"])
+        c5 = measure(ws, "lognormal_int4", args.steps, args.warmup, world, rank, local, device, e2e=False,
+                     equal_counts=False, min_timed_s=0.25)
+        lds = c5["loads"]
+        sharded_fig = {
+            "workload": "lognormal_int4", "desc": ws["desc"], "scaling": "strong",
+            "value": round(c5["value"], 1), "unit": "GB/s", "ms_per_step": c5["ms"] / c5["steps"],
+            "steps": c5["steps"], "timed_repeats": c5["repeats"],
+            "attention_avg_launch_ms": c5["att_avg_ms"],
+            "gather_ms_per_step": round(c5["gather_ms"], 4) if world > 1 else None,
+            "rank_token_loads": lds, "load_max_over_mean": round(max(lds) / (sum(lds) / len(lds)), 4),
+            "split": "LPT on context length (token-balanced, unequal sequence counts); padded all-gather of the "
+                     "last layer's outputs plus per-rank lengths",
+            "clocks": c5["clk"]}
+        c5["cache"] = c5["q"] = None
+        torch.cuda.empty_cache()
 
     if rank == 0:
         peak, peak_kind = peaks()
-        achieved = att_bytes_per_launch / (att_avg_ms / 1e3) / 1e9
-        value = tot_step_bytes / (ms / args.steps / 1e3) / 1e9
-        tok_s = tot_batch * args.steps / (ms / 1e3)
+        L = m["L"]
+        achieved = m["att_bytes_per_launch"] / (m["att_avg_ms"] / 1e3) / 1e9
+        seq_steps = m["tot_batch"] * args.steps / (m["ms"] / 1e3)
+        kernel = "paged_decode_tma_kernel" if os.environ.get("METAGROSS_B200_ATTENTION") != "registers" \
+            else "paged_decode_kernel"
         line = {
-            "metric": metric, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-            "scaling": "strong" if sharded else "weak",
+            "metric": metric, "value": round(m["value"], 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": m["ms"] / args.steps, "higher_is_better": True,
+            "scaling": "strong" if m["sharded"] else "weak",
             "vs_baseline": None, "dtype": w["kv"] if w["kv"] == "int8" else "int4", "data": "synthetic",
-            "config": {"workload": args.workload, "desc": w["desc"], "global_batch": int(tot_batch),
-                       "context_mean": round(ctx_mean, 1), "truncations_timed": n_trunc,
+            "config": {"workload": args.workload, "desc": w["desc"], "global_batch": int(m["tot_batch"]),
+                       "context_mean": round(m["ctx_mean"], 1), "truncations_timed": m["n_trunc"],
                        "layers": L, "parallelism": f"sequence-sharded dp{world}",
                        "l2": "working set per step > 126 MB L2 (one pool per layer); no flush"},
-            "decode_tokens_per_s": round(tok_s, 1),
-            "bytes_per_step": tot_step_bytes,
+            "timed_repeats": m["repeats"], "ms_per_repeat": m["ms_per_repeat"],
+            "sequence_steps_per_s": round(seq_steps, 1),
+            "bytes_per_step": m["tot_step_bytes"],
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "traffic": traffic_per_launch(args.workload),
-                         "kernel": "paged_decode_kernel", "algorithmic_bytes_per_launch": att_bytes_per_launch,
-                         "avg_launch_ms": att_avg_ms,
+                         "kernel": kernel, "algorithmic_bytes_per_launch": m["att_bytes_per_launch"],
+                         "avg_launch_ms": m["att_avg_ms"],
                          "timing": f"graph of the {L} attention launches (one per layer pool), CUDA events, "
-                                   f"{att_reps} replays"},
-            "e2e": e2e,
-            "gather_ms_per_step": round(gather_ms, 4) if world > 1 else None,
-            "gpu_launches": args.steps * (2 + 2 * L) + n_trunc,
-            "clocks": clk,
+                                   f"{m['att_reps']} replays"},
+            "e2e": {"value": round(m["tot_e_bytes"] / (m["e_ms"] / 1e3) / 1e9, 1), "unit": "GB/s",
+                    "h2d_bytes_per_step": m["e2e_io"][0], "d2h_bytes_per_step": m["e2e_io"][1],
+                    "ms_per_step": m["e_ms"] / m["e2e_steps"]},
+            "gather_ms_per_step": round(m["gather_ms"], 4) if world > 1 else None,
+            "gpu_launches": m["repeats"] * args.steps * (2 + 2 * L) + m["n_trunc"],
+            "clocks": m["clk"],
         }
+        if ref_cuda is not None:
+            if "ms_per_step" in ref_cuda:
+                ref_cuda["value"] = round(m["tot_step_bytes"] / (ref_cuda["ms_per_step"] / 1e3) / 1e9, 1)
+                ref_cuda["step_speedup_of_this_line"] = round(ref_cuda["ms_per_step"] / (m["ms"] / args.steps), 1)
+            line["reference_cuda"] = ref_cuda
+        if sharded_fig is not None:
+            line["sharded_lognormal_int4"] = sharded_fig
         if world == 1 and not args.no_cpu_baseline:
             gbs, cores, sample = cpu_sample_gbs(w, seconds=args.cpu_seconds)
             line["cpu_baseline"] = {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample}
+            sys.path.insert(0, os.path.join(ROOT, "oracle"))
+            import oracle_cpu
+
+            c1, c1_threads, c1_desc, c1_ms = oracle_cpu.time_cpu_reference_config(
+                seconds=max(2.0, min(args.cpu_seconds, 10.0)))
+            line["cpu_baseline_reference_config"] = {"value": round(c1, 4), "unit": "GB/s", "ms_per_step": c1_ms,
+                                                     "cores": c1_threads, "kind": "port", "sample": c1_desc}
         print(json.dumps(line), flush=True)
 
     if world > 1:

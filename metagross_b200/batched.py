@@ -80,6 +80,8 @@ class BatchedPagedKVCache:
         self.scale_granularity = scale_granularity
         self.staging_dtype = staging_dtype
         self.device = torch.device(device)
+        if self.device.type == "cuda" and self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
         self.max_blocks = int(max_blocks) if max_blocks else 64
         self.num_pages = int(num_pages) if num_pages else batch * self.max_blocks
         row = head_dim if kv_dtype == "int8" else head_dim // 2

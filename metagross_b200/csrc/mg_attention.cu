@@ -2,7 +2,14 @@
 // entry points (mg_paged_attention_committed, mg_paged_decode_attention).
 // The kernel and its design notes are in mg_attention.cuh /
 // mg_attention_kernel.cuh.
+#include <cudaTypedefs.h>
+
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
 #include "mg_attention.cuh"
+#include "mg_attention_tma.cuh"
 
 namespace mg {
 namespace {
@@ -91,6 +98,154 @@ mg_status make_decode_plan(int kv4, int hd, int P, int Hkv, int Hq, int q_f16, i
 }
 
 namespace {
+
+// ---------------------------------------------------------------------------
+// bulk-copy kernel: which calls it serves, its shape, and its tensor maps
+// ---------------------------------------------------------------------------
+constexpr int64_t kTmaSmemLimit = 232448 - 1024;  // 227 KB per CTA, less the static arrays and slack
+
+// The layout the bulk-copy kernel implements (mg_attention_tma.cuh); the
+// environment variable METAGROSS_B200_ATTENTION=registers selects the
+// register-streaming kernel for every call instead.
+bool tma_applies(const mg_cache_layout* L, bool staged) {
+    const char* sel = std::getenv("METAGROSS_B200_ATTENTION");
+    if (sel && std::strcmp(sel, "registers") == 0) return false;
+    return L->page_size == 16 && L->scale_layout == MG_SCALE_PAGE && (!staged || L->staging_dtype == MG_F16) &&
+           (L->head_dim == 64 || L->head_dim == 128) && L->num_kv_heads >= 1 && L->num_kv_heads <= 15;
+}
+
+// Shape of the bulk-copy kernel for a plan `base` of the register kernel (same
+// work split, workspace and query-column layout).  False when the pages do not
+// fit two stages.
+bool make_tma_plan(const DecodePlan& base, int kv4, int hd, int Hkv, DecodePlan* out, DecodeParams* p) {
+    if (hd == 128 && base.nt > 1) return false;  // two n-tiles of head_dim 128 exceed 128 registers
+    DecodePlan pl = base;
+    const int wph = Hkv > 12 ? 1 : 12 / Hkv;  // consumer warps: 12, or one per kv head for 13-15
+    pl.hpw = 1;
+    pl.wph = wph;
+    pl.nconsumers = Hkv * wph;
+    pl.nwarps = pl.nconsumers + 1;
+    const int64_t rowb = kv4 ? hd / 2 : hd;
+    const int64_t page = 16 * Hkv * rowb;
+    const int64_t half = align_up(page, 1024);
+    const int ncols = pl.split_mode ? 1 : 2;
+    const int64_t prefix = align_up(static_cast<int64_t>(kRecCache) * 32 + kPlanPids * 4, 128);
+    const int64_t scratch = wph > 1 ? align_up(static_cast<int64_t>(pl.nconsumers) * pl.nt * ncols * 4 * (hd + 2) * 4, 128) : 0;
+    int nsl = 6;
+    int64_t bar_off = 0, meta_off = 0, stage_off = 0;
+    for (; nsl >= 1; --nsl) {
+        const int64_t ns = 1ll << nsl;
+        bar_off = prefix + scratch;
+        meta_off = bar_off + 2 * ns * 8;
+        stage_off = align_up(meta_off + ns * 8, 1024);
+        if (1024 + stage_off + ns * 2 * half <= kTmaSmemLimit) break;
+    }
+    if (nsl < 1) return false;
+    pl.scratch_off = static_cast<int>(prefix);
+    pl.tail_off = 0;
+    pl.tail_slot = 0;
+    pl.smem_bytes = 1024 + stage_off + (1ll << nsl) * 2 * half;
+    p->nconsumers = pl.nconsumers;
+    p->wph = pl.wph;
+    p->scratch_off = pl.scratch_off;
+    p->tma_nsl = nsl;
+    p->tma_stage_bytes = static_cast<int>(2 * half);
+    p->tma_stage_off = static_cast<int>(stage_off);
+    p->tma_bar_off = static_cast<int>(bar_off);
+    p->tma_meta_off = static_cast<int>(meta_off);
+    *out = pl;
+    return true;
+}
+
+// Tensor maps of page pools, encoded once per (pool, shape, device).  A pool
+// [N, 16, Hkv, rowb] is described as the 4-D tensor (rowb, token, kv head,
+// page) with strides (Hkv*rowb, rowb, page bytes) -- the box (rowb, 16, Hkv, 1)
+// lands one page as [kv head][token][rowb] -- or, where the driver declines
+// those strides, as the 3-D tensor (rowb, kv head, token of the pool) copied one
+// kv head at a time.  16-byte chunks are swizzled within 32/64/128-byte rows.
+struct PageMapKey {
+    const void* pool;
+    int64_t n;
+    int hkv, rowb, dev;
+    bool operator==(const PageMapKey& o) const {
+        return pool == o.pool && n == o.n && hkv == o.hkv && rowb == o.rowb && dev == o.dev;
+    }
+};
+struct PageMapEntry {
+    PageMapKey key;
+    CUtensorMap map;
+    int per_head;
+    bool used;
+};
+
+mg_status page_tensor_map(const void* pool, int64_t n, int hkv, int rowb, CUtensorMap* out, int* per_head) {
+    static PageMapEntry cache[128];
+    static int next = 0;
+    static std::mutex mu;
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const PageMapKey key{pool, n, hkv, rowb, dev};
+    std::lock_guard<std::mutex> lock(mu);
+    for (auto& e : cache)
+        if (e.used && e.key == key) {
+            *out = e.map;
+            *per_head = e.per_head;
+            return MG_OK;
+        }
+    if (!encode) {
+        cudaDriverEntryPointQueryResult q;
+        void* fn = nullptr;
+        const cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+            return set_error(MG_ERR_CUDA, "cuTensorMapEncodeTiled unavailable: %s", cudaGetErrorString(e));
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    const CUtensorMapSwizzle sw = rowb == 32   ? CU_TENSOR_MAP_SWIZZLE_32B
+                                  : rowb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                               : CU_TENSOR_MAP_SWIZZLE_128B;
+    const cuuint64_t page = 16ull * hkv * rowb;
+    CUtensorMap m;
+    int ph = 0;
+    {
+        const cuuint64_t dims[4] = {static_cast<cuuint64_t>(rowb), 16, static_cast<cuuint64_t>(hkv),
+                                    static_cast<cuuint64_t>(n)};
+        const cuuint64_t strides[3] = {static_cast<cuuint64_t>(hkv) * rowb, static_cast<cuuint64_t>(rowb), page};
+        const cuuint32_t box[4] = {static_cast<cuuint32_t>(rowb), 16, static_cast<cuuint32_t>(hkv), 1};
+        const cuuint32_t es[4] = {1, 1, 1, 1};
+        const CUresult r = encode(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(pool), dims, strides, box,
+                                  es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) ph = 1;
+    }
+    if (ph) {
+        const cuuint64_t dims[3] = {static_cast<cuuint64_t>(rowb), static_cast<cuuint64_t>(hkv),
+                                    static_cast<cuuint64_t>(n) * 16};
+        const cuuint64_t strides[2] = {static_cast<cuuint64_t>(rowb), static_cast<cuuint64_t>(hkv) * rowb};
+        const cuuint32_t box[3] = {static_cast<cuuint32_t>(rowb), 1, 16};
+        const cuuint32_t es[3] = {1, 1, 1};
+        const CUresult r = encode(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(pool), dims, strides, box,
+                                  es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return set_error(MG_ERR_CUDA, "cuTensorMapEncodeTiled(page pool) failed: %d", (int)r);
+    }
+    PageMapEntry& e = cache[next];
+    next = (next + 1) % 128;
+    e.key = key;
+    e.map = m;
+    e.per_head = ph;
+    e.used = true;
+    *out = m;
+    *per_head = ph;
+    return MG_OK;
+}
+
+// A batched call's kernel: the bulk-copy one when `use`.
+struct TmaLaunch {
+    bool use = false;
+    DecodePlan pl;
+    CUtensorMap tk, tv;
+};
 
 void fill_common(DecodeParams& p, const DecodePlan& pl, int P, int Hkv, int Hq, int hd, int kv4, double scale,
                  int64_t num_pages, int batch) {
@@ -226,7 +381,7 @@ namespace {
 mg_status prepare_batched(const mg_cache_layout* L, const mg_layer_ptrs* lp, const int32_t* block_tables, int32_t batch,
                           const void* q, int32_t q_dtype, int32_t num_q_heads, float scale, void* out,
                           int32_t out_dtype, void* workspace, int64_t workspace_bytes, int32_t* dev_status,
-                          DecodeParams* pp, DecodePlan* plp) {
+                          DecodeParams* pp, DecodePlan* plp, TmaLaunch* tl) {
     mg_status st = check_cache_layout(L);
     if (st != MG_OK) return st;
     MG_REQUIRE(lp && lp->k_pool && lp->v_pool && lp->k_scales && lp->v_scales, "null layer pointer");
@@ -269,9 +424,28 @@ mg_status prepare_batched(const mg_cache_layout* L, const mg_layer_ptrs* lp, con
     p.out_wv = nullptr;
     p.status = dev_status;
     set_workspace(p, pl, num_q_heads, L->head_dim, workspace);
+    tl->use = false;
+    if (tma_applies(L, staged) && make_tma_plan(pl, L->kv_dtype == MG_KV_INT4, L->head_dim, L->num_kv_heads, &tl->pl, &p)) {
+        const int rowb = L->kv_dtype == MG_KV_INT4 ? L->head_dim / 2 : L->head_dim;
+        int ph_k = 0, ph_v = 0;
+        st = page_tensor_map(lp->k_pool, L->num_pages, L->num_kv_heads, rowb, &tl->tk, &ph_k);
+        if (st != MG_OK) return st;
+        st = page_tensor_map(lp->v_pool, L->num_pages, L->num_kv_heads, rowb, &tl->tv, &ph_v);
+        if (st != MG_OK) return st;
+        MG_REQUIRE(ph_k == ph_v, "K and V pools got different tensor-map forms");
+        p.tma_per_head = ph_k;
+        tl->use = true;
+    }
     *pp = p;
     *plp = pl;
     return MG_OK;
+}
+
+mg_status launch_any(int kv4, int hd, const DecodeParams& p, const DecodePlan& pl, const TmaLaunch& tl,
+                     cudaStream_t s) {
+    if (!tl.use) return launch(kv4, hd, p, pl, s);
+    if (kv4) return hd == 64 ? launch_tma<true, 64>(p, tl.pl, tl.tk, tl.tv, s) : launch_tma<true, 128>(p, tl.pl, tl.tk, tl.tv, s);
+    return hd == 64 ? launch_tma<false, 64>(p, tl.pl, tl.tk, tl.tv, s) : launch_tma<false, 128>(p, tl.pl, tl.tk, tl.tv, s);
 }
 
 }  // namespace
@@ -302,12 +476,13 @@ extern "C" mg_status mg_paged_decode_attention_planned(const mg_cache_layout* L,
     if (batch == 0) return MG_OK;
     DecodeParams p;
     DecodePlan pl;
+    TmaLaunch tl;
     mg_status st = prepare_batched(L, lp, block_tables, batch, q, q_dtype, num_q_heads, scale, out, out_dtype,
-                                   workspace, workspace_bytes, dev_status, &p, &pl);
+                                   workspace, workspace_bytes, dev_status, &p, &pl, &tl);
     if (st != MG_OK) return st;
     MG_REQUIRE(plan && aligned16(plan) && plan_bytes >= p.lay.words * 4, "decode plan missing, unaligned or too small");
     p.plan = static_cast<const int32_t*>(plan);
-    return launch(L->kv_dtype == MG_KV_INT4, L->head_dim, p, pl, as_stream(stream));
+    return launch_any(L->kv_dtype == MG_KV_INT4, L->head_dim, p, pl, tl, as_stream(stream));
 }
 
 extern "C" mg_status mg_paged_decode_attention(const mg_cache_layout* L, const mg_layer_ptrs* lp,
@@ -321,8 +496,9 @@ extern "C" mg_status mg_paged_decode_attention(const mg_cache_layout* L, const m
     MG_REQUIRE(seq_lens, "null pointer");
     DecodeParams p;
     DecodePlan pl;
+    TmaLaunch tl;
     mg_status st = prepare_batched(L, lp, block_tables, batch, q, q_dtype, num_q_heads, scale, out, out_dtype,
-                                   workspace, workspace_bytes, dev_status, &p, &pl);
+                                   workspace, workspace_bytes, dev_status, &p, &pl, &tl);
     if (st != MG_OK) return st;
     MG_REQUIRE(workspace_bytes >= pl.ws_bytes, "workspace too small: %lld < %lld bytes", (long long)workspace_bytes,
                (long long)pl.ws_bytes);
@@ -331,5 +507,5 @@ extern "C" mg_status mg_paged_decode_attention(const mg_cache_layout* L, const m
                             pl.ws_bytes - pl.plan_off, dev_status, as_stream(stream));
     if (st != MG_OK) return st;
     p.plan = plan;
-    return launch(L->kv_dtype == MG_KV_INT4, L->head_dim, p, pl, as_stream(stream));
+    return launch_any(L->kv_dtype == MG_KV_INT4, L->head_dim, p, pl, tl, as_stream(stream));
 }

@@ -136,6 +136,14 @@ struct DecodeParams {
     float* ws_l;    // [2*G, Hq]
     uint32_t* tickets;  // [batch]
     int32_t* status;
+    // bulk-copy kernel (mg_attention_tma.cuh): dynamic shared memory layout,
+    // offsets from the 1024-byte aligned base
+    int tma_nsl;          // log2 of the stage count
+    int tma_stage_bytes;  // one stage: K page, then V page at half of it
+    int tma_stage_off;
+    int tma_bar_off;      // full[NS], empty[NS] mbarriers
+    int tma_meta_off;     // per stage (K scale, V scale)
+    int tma_per_head;     // the tensor maps are 3-D, one copy per kv head
 };
 
 struct DecodePlan {

@@ -139,3 +139,97 @@ def time_decode_sample(w, seconds=10.0, seed=0, max_seqs=8):
               f"(append + dequantize-then-attend fp32 numpy) in {el:.1f} s; {threads} BLAS threads on {cores} "
               f"host cores")
     return gbs, threads, sample
+
+
+# --------------------------------------------------------------------------
+# The CPU reference configuration itself: batch 4, 12 heads, head_dim 64,
+# page 16, contexts U[1, 512], fp32 N(0, 1), INT8 with one absmax scale per
+# (token, head) vector, shuffled physical pages, one decode step.
+# --------------------------------------------------------------------------
+
+def _quantize_rows_int8(x):
+    """tests/reference.py:4-11 ``quantize_symmetric_int8`` applied to every
+    last-axis vector of ``x`` at once: scale = absmax / 127 (1e-8 when the
+    absmax is <= 1e-12), codes = clip(round-half-even(x / scale), -127, 127)."""
+    a = np.abs(x).max(axis=-1, keepdims=True)
+    s = np.where(a > 1e-12, a / 127.0, 1e-8)
+    q = np.clip(np.round(x / s), -127, 127).astype(np.int8)
+    return q, s[..., 0]
+
+
+def _dequantize_rows_int8(q, s):
+    """tests/reference.py:14-15 ``dequantize_symmetric_int8``: codes as float32
+    times float32(scale), per vector."""
+    return q.astype(np.float32) * s.astype(np.float32)[..., None]
+
+
+def time_cpu_reference_config(seconds=10.0, seed=0):
+    """One decode step of the CPU reference configuration, repeated until
+    ``seconds`` pass: per sequence, quantize the new token's K and V vectors
+    (per token and head), dequantize the cached codes through the shuffled
+    block table, and run fp32 attention in torch on the CPU (scores by einsum,
+    max-subtracted softmax, einsum with V: the steps of
+    tests/test_attention.py:14-20).  Returns (GB/s over the bytes the step
+    reads and writes -- codes and per-(token, head) scales of the cache, the new
+    token, q and out -- threads, description)."""
+    import torch
+
+    rng = np.random.default_rng(seed)
+    B, H, D, P = 4, 12, 64, 16
+    ctx = rng.integers(1, 513, size=B)
+    nblocks = [int(c + 1 + P - 1) // P for c in ctx]
+    num_pages = sum(nblocks) + 8
+    perm = rng.permutation(num_pages)
+    codes_k = np.zeros((num_pages, P, H, D), np.int8)
+    codes_v = np.zeros_like(codes_k)
+    sc_k = np.zeros((num_pages, P, H), np.float64)
+    sc_v = np.zeros_like(sc_k)
+    tables, nxt = [], 0
+    for b in range(B):
+        tables.append(perm[nxt:nxt + nblocks[b]])
+        nxt += nblocks[b]
+    lens = [int(c) for c in ctx]
+    for b in range(B):
+        x = rng.standard_normal((lens[b], H, D)).astype(np.float32)
+        y = rng.standard_normal((lens[b], H, D)).astype(np.float32)
+        qk, sk = _quantize_rows_int8(x)
+        qv, sv = _quantize_rows_int8(y)
+        for t in range(lens[b]):
+            pg, off = tables[b][t // P], t % P
+            codes_k[pg, off], sc_k[pg, off] = qk[t], sk[t]
+            codes_v[pg, off], sc_v[pg, off] = qv[t], sv[t]
+    q = [torch.from_numpy(rng.standard_normal((H, D)).astype(np.float32)) for _ in range(B)]
+    new_k = rng.standard_normal((B, H, D)).astype(np.float32)
+    new_v = rng.standard_normal((B, H, D)).astype(np.float32)
+    inv = 1.0 / np.sqrt(D)
+    steps = 0
+    t0 = time.perf_counter()
+    total = 0.0
+    while True:
+        for b in range(B):
+            c = lens[b]  # the step appends token c, then attends over c + 1 tokens
+            pg, off = tables[b][c // P], c % P
+            codes_k[pg, off], sc_k[pg, off] = _quantize_rows_int8(new_k[b])
+            codes_v[pg, off], sc_v[pg, off] = _quantize_rows_int8(new_v[b])
+            n = c + 1
+            tb = tables[b][: (n + P - 1) // P]
+            k = _dequantize_rows_int8(codes_k[tb], sc_k[tb]).reshape(-1, H, D)[:n]
+            v = _dequantize_rows_int8(codes_v[tb], sc_v[tb]).reshape(-1, H, D)[:n]
+            kt, vt = torch.from_numpy(k), torch.from_numpy(v)
+            s = torch.einsum("thd,hd->ht", kt, q[b]) * inv
+            s = s - s.max(dim=-1, keepdim=True).values
+            pr = torch.softmax(s, dim=-1)
+            torch.einsum("ht,thd->hd", pr, vt)
+            total += 2 * n * H * (D + 4) + 2 * H * (D * 4 + D + 4) + 2 * H * D * 4
+        steps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    gbs = total / el / 1e9
+    threads = max(_blas_threads(), torch.get_num_threads())
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    desc = (f"CPU reference configuration: batch 4, 12 heads, head_dim 64, page 16, contexts "
+            f"{int(ctx.min())}..{int(ctx.max())} (U[1, 512]), fp32, INT8 per-(token, head) scales, shuffled pages; "
+            f"{steps} decode steps (quantize the new token, dequantize, fp32 torch attention) in {el:.1f} s, "
+            f"ms/step {1e3 * el / steps:.3f}; {threads} threads on {cores} host cores")
+    return gbs, threads, desc, 1e3 * el / steps

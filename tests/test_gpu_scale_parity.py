@@ -15,10 +15,14 @@ sequence on its own SMs).  These cases cover what the benchmarks exercise:
 * the CUDA-graph decode step (DecodeGraph) replayed across page commits and
   an eager truncation, against the same steps run eagerly and the oracle.
 
-Parity bar: max-abs <= 2e-3 of the float64 dequantize-then-attend oracle for
-fp16 outputs (tests/test_attention.py:14-20 of the reference over read_fp32,
-with the log-sum-exp merge of metagross/attention.py:15-26 for the staged
-tail); cache state (codes, scales, block tables, free list) bit-exact.
+Parity bar: |out - ref| <= 2e-3 + 2^-11 |ref| elementwise against the
+float64 dequantize-then-attend oracle (tests/test_attention.py:14-20 of the
+reference over read_fp32, with the log-sum-exp merge of
+metagross/attention.py:15-26 for the staged tail).  2^-11 |ref| is the
+rounding of an fp16 output itself: with 1 % of the K/V elements scaled by 8,
+some outputs reach |16|, where fp16 values are 2^-6 apart, so no fp16 output
+can be within a flat 2e-3 of them.  Cache state (codes, scales, block tables,
+free list) bit-exact.
 """
 import numpy as np
 import pytest
@@ -29,6 +33,12 @@ import oracle as O
 pytestmark = pytest.mark.gpu
 
 TOL = 2e-3
+
+
+def _excess(out, ref):
+    """max over elements of |out - ref| - 2^-11 |ref| (the fp16 rounding of ref)."""
+    out = out.float().cpu().numpy() if isinstance(out, torch.Tensor) else out
+    return float((np.abs(out - ref) - np.abs(ref) * 2.0 ** -11).max())
 
 
 def _cache_cls():
@@ -114,7 +124,7 @@ def test_stream_k_lognormal_int4_gqa_matches_oracle():
     o = out.float().cpu().numpy()
     empty = lens == 0
     assert np.all(o[empty] == 0.0)
-    err = np.abs(o - ref).max(axis=(1, 2))
+    err = (np.abs(o - ref) - np.abs(ref) * 2.0 ** -11).max(axis=(1, 2))
     assert err.max() < TOL, (int(err.argmax()), float(err.max()), int(lens[err.argmax()]))
     # a second call on the same plan: the merge tickets were left at zero
     out2 = cache.attend(0, q.cuda())
@@ -138,7 +148,7 @@ def test_tinyllama_shape_int4_full_size_matches_oracle():
     torch.cuda.synchronize()
     cache.check()
     assert _plan_mode(cache) == 1
-    err = np.abs(out.float().cpu().numpy() - model.attend(q.float().numpy(), 1.0 / 8)).max()
+    err = _excess(out, model.attend(q.float().numpy(), 1.0 / 8))
     assert err < TOL, err
 
 
@@ -159,7 +169,7 @@ def test_gpt2_shape_int8_full_size_matches_oracle():
     out = cache.attend(0, q.cuda())
     torch.cuda.synchronize()
     cache.check()
-    err = np.abs(out.float().cpu().numpy() - model.attend(q.float().numpy(), 1.0 / 8)).max()
+    err = _excess(out, model.attend(q.float().numpy(), 1.0 / 8))
     assert err < TOL, err
     # one more decode token per sequence: a staged tail of 1 row beside 64 pages
     k = torch.randn(B, 1, H, D, generator=g).half()
@@ -170,7 +180,7 @@ def test_gpt2_shape_int8_full_size_matches_oracle():
     out = cache.attend(0, q.cuda())
     torch.cuda.synchronize()
     cache.check()
-    err = np.abs(out.float().cpu().numpy() - model.attend(q.float().numpy(), 1.0 / 8)).max()
+    err = _excess(out, model.attend(q.float().numpy(), 1.0 / 8))
     assert err < TOL, err
 
 
@@ -226,7 +236,7 @@ def test_decode_graph_replays_match_eager_steps_and_oracle(kv):
         for layer in range(Lyr):
             assert torch.equal(out[layer], eager[layer]), (step, layer)
             ref = models[layer].attend(qs[layer].float().numpy(), 1.0 / 8)
-            err = np.abs(out[layer].float().cpu().numpy() - ref).max()
+            err = _excess(out[layer], ref)
             assert err < TOL, (step, layer, err)
         if step == 12:
             # eager truncation on both caches: a page boundary, inside the
