@@ -104,12 +104,18 @@ namespace {
 // ---------------------------------------------------------------------------
 constexpr int64_t kTmaSmemLimit = 232448 - 1024;  // 227 KB per CTA, less the static arrays and slack
 
-// The layout the bulk-copy kernel implements (mg_attention_tma.cuh); the
-// environment variable METAGROSS_B200_ATTENTION=registers selects the
-// register-streaming kernel for every call instead.
+// The layout the bulk-copy kernel serves (mg_attention_tma.cuh): INT8 pages.
+// INT4 pages of the TinyLlama attention shape are 2 KB per K or V copy, and
+// streams of 2 KB copies measured 0.9-1.7 TB/s (a per-SM rate of copies, not
+// of bytes) against 5-6 TB/s for 12 KB pages, so the register-streaming kernel
+// serves INT4 (it measured 395 against 520-606 us on the 1024-sequence
+// log-normal INT4 launch).  The environment variable
+// METAGROSS_B200_ATTENTION=registers selects the register kernel for every
+// call, =bulk the bulk-copy kernel for INT4 pools too.
 bool tma_applies(const mg_cache_layout* L, bool staged) {
     const char* sel = std::getenv("METAGROSS_B200_ATTENTION");
     if (sel && std::strcmp(sel, "registers") == 0) return false;
+    if (L->kv_dtype == MG_KV_INT4 && !(sel && std::strcmp(sel, "bulk") == 0)) return false;
     return L->page_size == 16 && L->scale_layout == MG_SCALE_PAGE && (!staged || L->staging_dtype == MG_F16) &&
            (L->head_dim == 64 || L->head_dim == 128) && L->num_kv_heads >= 1 && L->num_kv_heads <= 15;
 }
@@ -131,24 +137,26 @@ bool make_tma_plan(const DecodePlan& base, int kv4, int hd, int Hkv, DecodePlan*
     const int ncols = pl.split_mode ? 1 : 2;
     const int64_t prefix = align_up(static_cast<int64_t>(kRecCache) * 32 + kPlanPids * 4, 128);
     const int64_t scratch = wph > 1 ? align_up(static_cast<int64_t>(pl.nconsumers) * pl.nt * ncols * 4 * (hd + 2) * 4, 128) : 0;
-    int nsl = 6;
+    // the deepest ring (up to 64 stages) that fits; a consumer warp holds two of
+    // its pages (WPH apart) at once, so the ring must be deeper than that span
+    int ns = 64;
     int64_t bar_off = 0, meta_off = 0, stage_off = 0;
-    for (; nsl >= 1; --nsl) {
-        const int64_t ns = 1ll << nsl;
+    for (; ns > 2 * wph; --ns) {
         bar_off = prefix + scratch;
         meta_off = bar_off + 2 * ns * 8;
         stage_off = align_up(meta_off + ns * 8, 1024);
         if (1024 + stage_off + ns * 2 * half <= kTmaSmemLimit) break;
     }
-    if (nsl < 1) return false;
+    if (ns <= 2 * wph) return false;
     pl.scratch_off = static_cast<int>(prefix);
     pl.tail_off = 0;
     pl.tail_slot = 0;
-    pl.smem_bytes = 1024 + stage_off + (1ll << nsl) * 2 * half;
+    pl.smem_bytes = 1024 + stage_off + static_cast<int64_t>(ns) * 2 * half;
     p->nconsumers = pl.nconsumers;
     p->wph = pl.wph;
     p->scratch_off = pl.scratch_off;
-    p->tma_nsl = nsl;
+    p->tma_ns = ns;
+    p->tma_nsdiv = FastDiv(static_cast<uint32_t>(ns));
     p->tma_stage_bytes = static_cast<int>(2 * half);
     p->tma_stage_off = static_cast<int>(stage_off);
     p->tma_bar_off = static_cast<int>(bar_off);

@@ -5,10 +5,11 @@
 // metagross/attention.py:62-134 (exact staged tail merged with a log-sum-exp
 // merge, then normalised).  Here one kernel does all of it for a batch:
 //
-//   work    stream-K over the flattened list of "units" (one committed page,
-//           or the staged tail, of one sequence): CTA c of G processes units
-//           [c*W/G, (c+1)*W/G), so every CTA streams the same number of pages
-//           whatever the context lengths.  A sequence cut by a CTA boundary
+//   work    the step's decode plan (mg_plan.cu): when the non-empty
+//           sequences fit on the SMs, each is cut into near-equal chunks, one
+//           per CTA; otherwise stream-K over the flattened list of "units" (one
+//           committed page, or the staged tail, of one sequence): CTA c of G
+//           processes units [c*W/G, (c+1)*W/G).  A sequence cut by a CTA boundary
 //           gets a partial (m, l, acc) from each covering CTA; the last of
 //           them to finish (atomic ticket, no waiting) merges and writes the
 //           output.  Each CTA writes at most two partials (its first and its
@@ -41,8 +42,11 @@
 //           in two mma columns (~22 mantissa bits).  Online softmax in the
 //           log2 domain with lazy rescaling (the running reference max moves
 //           only when a score exceeds it by 2^8).
-//   tail    the staged tokens are folded into the state on the CUDA cores in
-//           fp32 (scores of a chunk, then its exponentials and V sums).
+//   tail    an fp16 staged tail (< P exact rows) is one more 16-row tile on
+//           the tensor cores, its rows loaded straight into mma fragments; an
+//           fp32 tail (not exact in fp16) goes through a per-warp shared-memory
+//           ring and is folded in on the CUDA cores in fp32 (scores of a
+//           chunk, then its exponentials and V sums).
 #pragma once
 
 #include "mg_common.cuh"
@@ -138,7 +142,8 @@ struct DecodeParams {
     int32_t* status;
     // bulk-copy kernel (mg_attention_tma.cuh): dynamic shared memory layout,
     // offsets from the 1024-byte aligned base
-    int tma_nsl;          // log2 of the stage count
+    int tma_ns;           // stages in the ring
+    FastDiv tma_nsdiv;    // division by tma_ns (exact for page counters below 2^26)
     int tma_stage_bytes;  // one stage: K page, then V page at half of it
     int tma_stage_off;
     int tma_bar_off;      // full[NS], empty[NS] mbarriers

@@ -245,38 +245,46 @@ __device__ __forceinline__ void tma_clear(TmaHead<NT, MT>& S) {
     }
 }
 
-// Online-softmax update for one 16-token tile whose raw scores (K Q^T, code
-// offsets already removed) are sc[NT][4] (rows g, g + 8 x columns 2c, 2c + 1),
-// then O^T += V^T P^T over the m-tiles vf(mt, a) supplies.  ks0 / ks1: score
-// scales (log2 domain) of rows g / g + 8 (live0 / live1 mask dead rows); vs0 /
-// vs1 their V scales.  is16(mt): multiply P by 16 for that m-tile (tail tiles
-// of INT4 caches, whose V rows are not scaled by 16 as high-nibble codes are).
-template <int HD, int NT, bool SPLIT, typename VF, typename H16>
-__device__ __forceinline__ void tma_softmax_pv(TmaHead<NT, HD / 16>& S, float (&sc)[NT][4], VF&& vf, H16&& is16,
-                                               float ks0, float ks1, float vs0, float vs1, bool live0, bool live1) {
+// Online-softmax update for NTL 16-token tiles taken together, whose raw
+// scores (K Q^T, code offsets already removed) are sc[t][NT][4] (rows g, g + 8
+// x columns 2c, 2c + 1 of tile t), then O^T += V^T P^T over the m-tiles
+// vf(t, mt, a) supplies.  ks[t][r] / vs[t][r]: score scale (log2 domain) and V
+// scale of row g + 8 r of tile t; live[t][r] masks dead rows.  is16(mt):
+// multiply P by 16 for that m-tile (tail tiles of INT4 caches, whose V rows
+// are not scaled by 16 as high-nibble codes are).  With two tiles the warp
+// has two independent score chains in flight and pays one running-max check
+// for 32 tokens.
+template <int HD, int NT, bool SPLIT, int NTL, typename VF, typename H16>
+__device__ __forceinline__ void tma_softmax_pv(TmaHead<NT, HD / 16>& S, float (&sc)[NTL][NT][4], VF&& vf,
+                                               H16&& is16, const float (&ks)[NTL][2], const float (&vs)[NTL][2],
+                                               const bool (&live)[NTL][2]) {
     constexpr int MT = HD / 16;
     constexpr int NCOLS = SPLIT ? 1 : 2;
-    float s[NT][NCOLS][2];
+    float s[NTL][NT][NCOLS][2];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-        if (SPLIT) {
-            s[nt][0][0] = live0 ? (sc[nt][0] + sc[nt][1]) * ks0 : -INFINITY;
-            s[nt][0][1] = live1 ? (sc[nt][2] + sc[nt][3]) * ks1 : -INFINITY;
-        } else {
+    for (int t = 0; t < NTL; ++t)
 #pragma unroll
-            for (int col = 0; col < NCOLS; ++col) {
-                s[nt][col][0] = live0 ? sc[nt][col] * ks0 : -INFINITY;
-                s[nt][col][1] = live1 ? sc[nt][2 + col] * ks1 : -INFINITY;
+        for (int nt = 0; nt < NT; ++nt) {
+            if (SPLIT) {
+                s[t][nt][0][0] = live[t][0] ? (sc[t][nt][0] + sc[t][nt][1]) * ks[t][0] : -INFINITY;
+                s[t][nt][0][1] = live[t][1] ? (sc[t][nt][2] + sc[t][nt][3]) * ks[t][1] : -INFINITY;
+            } else {
+#pragma unroll
+                for (int col = 0; col < NCOLS; ++col) {
+                    s[t][nt][col][0] = live[t][0] ? sc[t][nt][col] * ks[t][0] : -INFINITY;
+                    s[t][nt][col][1] = live[t][1] ? sc[t][nt][2 + col] * ks[t][1] : -INFINITY;
+                }
             }
         }
-    }
     bool need = false;
     float mx[NT][NCOLS];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int col = 0; col < NCOLS; ++col) {
-            const float m = fmaxf(s[nt][col][0], s[nt][col][1]);
+            float m = fmaxf(s[0][nt][col][0], s[0][nt][col][1]);
+#pragma unroll
+            for (int t = 1; t < NTL; ++t) m = fmaxf(m, fmaxf(s[t][nt][col][0], s[t][nt][col][1]));
             mx[nt][col] = m;
             S.m_true[nt][col] = fmaxf(S.m_true[nt][col], m);
             need |= m > S.m_used[nt][col] + kRescaleThreshold;
@@ -306,67 +314,65 @@ __device__ __forceinline__ void tma_softmax_pv(TmaHead<NT, HD / 16>& S, float (&
                 }
             }
     }
-    uint32_t pb[NT][2];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-        float pr[NCOLS][2];
-#pragma unroll
-        for (int col = 0; col < NCOLS; ++col)
-#pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                pr[col][r] = ex2(s[nt][col][r] - S.m_used[nt][col]);
-                S.lpart[nt][col] += pr[col][r];
-            }
-        uint32_t hrow[2];
-        if (SPLIT) {
-            const float a0 = pr[0][0] * vs0, a1 = pr[0][1] * vs1;
-            const float a0h = __half2float(__float2half_rn(a0));
-            const float a1h = __half2float(__float2half_rn(a1));
-            hrow[0] = pack_half2(a0h, a0 - a0h);
-            hrow[1] = pack_half2(a1h, a1 - a1h);
-        } else {
-            hrow[0] = pack_half2(pr[0][0] * vs0, pr[NCOLS - 1][0] * vs0);
-            hrow[1] = pack_half2(pr[0][1] * vs1, pr[NCOLS - 1][1] * vs1);
-        }
-        pb[nt][0] = movmatrix_trans(hrow[0]);
-        pb[nt][1] = movmatrix_trans(hrow[1]);
-    }
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt) {
-        uint32_t a[4];
-        vf(mt, a);
+    for (int t = 0; t < NTL; ++t) {
+        uint32_t pb[NT][2];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-            if (is16(mt)) {
-                const uint32_t b0 = hfma2_u32(pb[nt][0], 0x4C004C00u, 0u), b1 = hfma2_u32(pb[nt][1], 0x4C004C00u, 0u);
-                mma_16816(S.acc[mt][nt], a, b0, b1);  // 0x4C00 = 16.0
+            float pr[NCOLS][2];
+#pragma unroll
+            for (int col = 0; col < NCOLS; ++col)
+#pragma unroll
+                for (int r = 0; r < 2; ++r) {
+                    pr[col][r] = ex2(s[t][nt][col][r] - S.m_used[nt][col]);
+                    S.lpart[nt][col] += pr[col][r];
+                }
+            uint32_t hrow[2];
+            if (SPLIT) {
+                const float a0 = pr[0][0] * vs[t][0], a1 = pr[0][1] * vs[t][1];
+                const float a0h = __half2float(__float2half_rn(a0));
+                const float a1h = __half2float(__float2half_rn(a1));
+                hrow[0] = pack_half2(a0h, a0 - a0h);
+                hrow[1] = pack_half2(a1h, a1 - a1h);
             } else {
-                mma_16816(S.acc[mt][nt], a, pb[nt][0], pb[nt][1]);
+                hrow[0] = pack_half2(pr[0][0] * vs[t][0], pr[NCOLS - 1][0] * vs[t][0]);
+                hrow[1] = pack_half2(pr[0][1] * vs[t][1], pr[NCOLS - 1][1] * vs[t][1]);
+            }
+            pb[nt][0] = movmatrix_trans(hrow[0]);
+            pb[nt][1] = movmatrix_trans(hrow[1]);
+        }
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+            uint32_t a[4];
+            vf(t, mt, a);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                if (is16(mt)) {
+                    const uint32_t b0 = hfma2_u32(pb[nt][0], 0x4C004C00u, 0u);  // 0x4C00 = 16.0
+                    const uint32_t b1 = hfma2_u32(pb[nt][1], 0x4C004C00u, 0u);
+                    mma_16816(S.acc[mt][nt], a, b0, b1);
+                } else {
+                    mma_16816(S.acc[mt][nt], a, pb[nt][0], pb[nt][1]);
+                }
             }
         }
     }
 }
 
-// One 16-token page tile of kv head h from a stage: K and V fragments by
-// ldmatrix (chunk offsets off[x] of this lane's matrix row), the stage is
-// released after the loads, then the math.
-template <bool KV4, int HD, int NT, bool SPLIT>
-__device__ __forceinline__ void tma_page_tile(TmaHead<NT, HD / 16>& S, uint32_t kbase, uint32_t vbase,
-                                              const uint32_t (&off)[TCfg<KV4, HD>::X4], float ks, float vs,
-                                              uint64_t* empty, int lane) {
+// Raw scores of one page tile in a stage (K fragments by ldmatrix at chunk
+// offsets off[x] of this lane's matrix row); INT8 offsets removed here.  CH2:
+// even and odd k-steps accumulate in two chains (shorter dependency, four more
+// registers).
+template <bool KV4, int HD, int NT, bool CH2>
+__device__ __forceinline__ void tma_tile_scores(const TmaHead<NT, HD / 16>& S, uint32_t kbase,
+                                                const uint32_t (&off)[TCfg<KV4, HD>::X4], float (&sc)[NT][4]) {
     using T = TCfg<KV4, HD>;
     constexpr int MT = T::MT;
-    uint32_t kr[T::X4][4], vr[T::X4][4];
+    uint32_t kr[T::X4][4];
 #pragma unroll
     for (int x = 0; x < T::X4; ++x) ldsm_x4(kr[x], kbase + off[x]);
-#pragma unroll
-    for (int x = 0; x < T::X4; ++x) ldsm_x4_t(vr[x], vbase + off[x]);
-    regs_ready(&kr[0][0], 4 * T::X4);
-    regs_ready(&vr[0][0], 4 * T::X4);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(empty);
     // kr[x] = {row g chunk 2x, row g+8 chunk 2x, row g chunk 2x+1, row g+8 chunk 2x+1}
-    float sc[NT][4], sc2[NT][4];
+    float sc2[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -402,44 +408,80 @@ __device__ __forceinline__ void tma_page_tile(TmaHead<NT, HD / 16>& S, uint32_t 
         }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-            if (kk & 1) mma_16816(sc2[nt], a, S.qf[nt][kk][0], S.qf[nt][kk][1]);
+            if (CH2 && (kk & 1)) mma_16816(sc2[nt], a, S.qf[nt][kk][0], S.qf[nt][kk][1]);
             else mma_16816(sc[nt], a, S.qf[nt][kk][0], S.qf[nt][kk][1]);
         }
     }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) sc[nt][i] = sc[nt][i] + sc2[nt][i] - S.qb[nt][i & 1];
-    tma_softmax_pv<HD, NT, SPLIT>(
-        S, sc,
-        [&](int mt, uint32_t (&a)[4]) {
-            // V codes without offsets (exact fp16 subtraction), so the
-            // accumulators never carry an offset x sum-of-P term across tiles
-            if (!KV4) {
-                // vr[mt >> 1] = {tokens 0-7 chunk 2p, 8-15 chunk 2p, 0-7 chunk 2p+1, 8-15 chunk 2p+1}
-                const uint32_t* r = vr[mt >> 1];
-                const int sh = (mt & 1) * 8;
-                a[0] = hsub2_u32(cvt8(r[0] >> sh), 0x64806480u);
-                a[1] = hsub2_u32(cvt8(r[2] >> sh), 0x64806480u);
-                a[2] = hsub2_u32(cvt8(r[1] >> sh), 0x64806480u);
-                a[3] = hsub2_u32(cvt8(r[3] >> sh), 0x64806480u);
-            } else {
-                // high nibbles come out as 16 c (1152 + 16 c - 1152): that m-tile's
-                // outputs are divided by 16 at the end
-                const uint32_t* r = vr[mt >> 2];
-                const int n = mt & 3;
-                uint32_t x[4];
+        for (int i = 0; i < 4; ++i) sc[nt][i] = (CH2 ? sc[nt][i] + sc2[nt][i] : sc[nt][i]) - S.qb[nt][i & 1];
+}
+
+// V^T A-fragment of m-tile mt from the ldmatrix.trans words vr of a page tile,
+// codes without offsets (exact fp16 subtraction), so the accumulators never
+// carry an offset x sum-of-P term across tiles.
+template <bool KV4, int HD>
+__device__ __forceinline__ void tma_vfrag(const uint32_t (&vr)[TCfg<KV4, HD>::X4][4], int mt, uint32_t (&a)[4]) {
+    if (!KV4) {
+        // vr[mt >> 1] = {tokens 0-7 chunk 2p, 8-15 chunk 2p, 0-7 chunk 2p+1, 8-15 chunk 2p+1}
+        const uint32_t* r = vr[mt >> 1];
+        const int sh = (mt & 1) * 8;
+        a[0] = hsub2_u32(cvt8(r[0] >> sh), 0x64806480u);
+        a[1] = hsub2_u32(cvt8(r[2] >> sh), 0x64806480u);
+        a[2] = hsub2_u32(cvt8(r[1] >> sh), 0x64806480u);
+        a[3] = hsub2_u32(cvt8(r[3] >> sh), 0x64806480u);
+    } else {
+        // high nibbles come out as 16 c (1152 + 16 c - 1152): that m-tile's
+        // outputs are divided by 16 at the end
+        const uint32_t* r = vr[mt >> 2];
+        const int n = mt & 3;
+        uint32_t x[4];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) x[i] = (r[i] ^ 0x88888888u) >> ((n >> 1) * 8);
-                const bool hi = n & 1;
-                const uint32_t off = hi ? 0x64806480u : 0x64086408u;
-                a[0] = hsub2_u32(hi ? hi4(x[0]) : lo4(x[0]), off);
-                a[1] = hsub2_u32(hi ? hi4(x[2]) : lo4(x[2]), off);
-                a[2] = hsub2_u32(hi ? hi4(x[1]) : lo4(x[1]), off);
-                a[3] = hsub2_u32(hi ? hi4(x[3]) : lo4(x[3]), off);
-            }
-        },
-        [](int) { return false; }, ks, ks, vs, vs, true, true);
+        for (int i = 0; i < 4; ++i) x[i] = (r[i] ^ 0x88888888u) >> ((n >> 1) * 8);
+        const bool hi = n & 1;
+        const uint32_t o = hi ? 0x64806480u : 0x64086408u;
+        a[0] = hsub2_u32(hi ? hi4(x[0]) : lo4(x[0]), o);
+        a[1] = hsub2_u32(hi ? hi4(x[2]) : lo4(x[2]), o);
+        a[2] = hsub2_u32(hi ? hi4(x[1]) : lo4(x[1]), o);
+        a[3] = hsub2_u32(hi ? hi4(x[3]) : lo4(x[3]), o);
+    }
+}
+
+// NTL (1 or 2) page tiles of kv head h from their stages: the scores of each,
+// then the V fragments; each stage is released once its V words are in
+// registers, then the softmax and O^T += V^T P^T for all of them.
+template <bool KV4, int HD, int NT, bool SPLIT, int NTL, bool CH2>
+__device__ __forceinline__ void tma_page_tiles(TmaHead<NT, HD / 16>& S, const uint32_t (&kbase)[NTL],
+                                               const uint32_t (&off)[TCfg<KV4, HD>::X4], uint32_t vdelta,
+                                               const float (&ksc)[NTL], const float (&vsc)[NTL],
+                                               uint64_t* const (&empty)[NTL], int lane) {
+    using T = TCfg<KV4, HD>;
+    float sc[NTL][NT][4];
+#pragma unroll
+    for (int t = 0; t < NTL; ++t) tma_tile_scores<KV4, HD, NT, CH2>(S, kbase[t], off, sc[t]);
+    uint32_t vr[NTL][T::X4][4];
+#pragma unroll
+    for (int t = 0; t < NTL; ++t)
+#pragma unroll
+        for (int x = 0; x < T::X4; ++x) ldsm_x4_t(vr[t][x], kbase[t] + vdelta + off[x]);
+    regs_ready(&vr[0][0][0], 4 * T::X4 * NTL);
+    __syncwarp();
+    if (lane == 0) {
+#pragma unroll
+        for (int t = 0; t < NTL; ++t) mbar_arrive(empty[t]);
+    }
+    float ks[NTL][2], vs[NTL][2];
+    bool live[NTL][2];
+#pragma unroll
+    for (int t = 0; t < NTL; ++t) {
+        ks[t][0] = ks[t][1] = ksc[t];
+        vs[t][0] = vs[t][1] = vsc[t];
+        live[t][0] = live[t][1] = true;
+    }
+    tma_softmax_pv<HD, NT, SPLIT, NTL>(
+        S, sc, [&](int t, int mt, uint32_t (&a)[4]) { tma_vfrag<KV4, HD>(vr[t], mt, a); }, [](int) { return false; },
+        ks, vs, live);
 }
 
 // The staged tail of kv head h of sequence b: rows 0 .. n - 1 (n < 16) of the
@@ -515,9 +557,16 @@ __device__ __forceinline__ void tma_tail_tile(TmaHead<NT, HD / 16>& S, const Dec
             }
         }
     }
-    tma_softmax_pv<HD, NT, SPLIT>(
-        S, sc,
-        [&](int mt, uint32_t (&a)[4]) {
+    float sct[1][NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sct[0][nt][i] = sc[nt][i];
+    const float ks[1][2] = {{p.sm_scale_log2, p.sm_scale_log2}}, vs[1][2] = {{1.0f, 1.0f}};
+    const bool live[1][2] = {{g < n, g + 8 < n}};
+    tma_softmax_pv<HD, NT, SPLIT, 1>(
+        S, sct,
+        [&](int, int mt, uint32_t (&a)[4]) {
             // A row g: dim(mt, 0), row g + 8: dim(mt, 1); k: tokens (2c, 2c+1) | (2c+8, 2c+9)
             int w0, w1, sel;
             if (!KV4) {
@@ -536,7 +585,7 @@ __device__ __forceinline__ void tma_tail_tile(TmaHead<NT, HD / 16>& S, const Dec
             a[2] = __byte_perm(vw[2][w0], vw[3][w0], pm);
             a[3] = __byte_perm(vw[2][w1], vw[3][w1], pm);
         },
-        [](int mt) { return KV4 && (mt & 1); }, p.sm_scale_log2, p.sm_scale_log2, 1.0f, 1.0f, g < n, g + 8 < n);
+        [](int mt) { return KV4 && (mt & 1); }, ks, vs, live);
 }
 
 template <bool KV4, int HD, int NT, bool SPLIT, int NW>

@@ -293,21 +293,24 @@ struct AppendParams {
 };
 
 // Code of 8 consecutive elements into the pool at element e of a page (INT8:
-// 8 bytes, INT4: 4 bytes of nibbles, the even element in the low nibble).
+// 8 bytes, INT4: 4 bytes of nibbles, the even element in the low nibble),
+// through quant_code_fast (the same codes as the IEEE quotient x / sf).
 template <bool INT4>
 __device__ __forceinline__ void store_codes(uint8_t* page_base, int64_t e, const float (&v)[8], float sf) {
+    const float inv = 1.0f / sf;
     if (!INT4) {
         uint32_t w0 = 0, w1 = 0;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            w0 |= (static_cast<uint32_t>(quant_code(v[i], sf, 127.0f)) & 0xFFu) << (8 * i);
-            w1 |= (static_cast<uint32_t>(quant_code(v[4 + i], sf, 127.0f)) & 0xFFu) << (8 * i);
+            w0 |= (static_cast<uint32_t>(quant_code_fast(v[i], sf, inv, 127.0f)) & 0xFFu) << (8 * i);
+            w1 |= (static_cast<uint32_t>(quant_code_fast(v[4 + i], sf, inv, 127.0f)) & 0xFFu) << (8 * i);
         }
         *reinterpret_cast<uint2*>(page_base + e) = make_uint2(w0, w1);
     } else {
         uint32_t w = 0;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) w |= (static_cast<uint32_t>(quant_code(v[i], sf, 7.0f)) & 0xFu) << (4 * i);
+        for (int i = 0; i < 8; ++i)
+            w |= (static_cast<uint32_t>(quant_code_fast(v[i], sf, inv, 7.0f)) & 0xFu) << (4 * i);
         *reinterpret_cast<uint32_t*>(page_base + e / 2) = w;
     }
 }

@@ -43,6 +43,21 @@ __device__ __forceinline__ int quant_code(float x, float s, float qmax) {
     return static_cast<int>(roundf(k));
 }
 
+// quant_code(x, s, qmax) with the quotient formed as x * inv, inv = 1 / s
+// rounded once.  x * inv is within 2^-23 |x / s| (plus its own rounding) of
+// the correctly rounded x / s, so the two round to the same integer unless the
+// quotient lies within a few ulps of a half-integer; only then is the IEEE
+// quotient taken.  Equal to quant_code for every input (NaN, infinities and the
+// clamp included): |x / s| <= qmax + 1 ulp whenever s = absmax / qmax covers x,
+// and a clamped quotient stays clamped.
+__device__ __forceinline__ int quant_code_fast(float x, float s, float inv, float qmax) {
+    if (isnan(x)) return 0;
+    const float q = x * inv;
+    const float f = fabsf(q - truncf(q));  // fractional part of |q|
+    if (fabsf(f - 0.5f) <= fabsf(q) * 4.8e-7f) return quant_code(x, s, qmax);
+    return static_cast<int>(roundf(fminf(qmax, fmaxf(-qmax, q))));
+}
+
 // scale = absmax / qmax in double (csrc/quantize.cu:108-109), 1e-8 when the
 // absmax is not finite or <= 1e-12.
 __device__ __forceinline__ double scale_from_absmax(float a, double qmax) {
@@ -255,9 +270,9 @@ __device__ __forceinline__ void grid_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 }
 
-// Fast unsigned division by a runtime divisor d in [1, 2^16) for n < 2^16:
-// q = (n * m) >> 16 ... kept simple: magic m = ceil(2^32 / d), q = umulhi(n, m).
-// Exact for n, d < 2^16 (error term n*(m*d - 2^32)/2^32/d < 1/d).
+// Fast unsigned division by a runtime divisor d in [1, 2^16): magic
+// m = ceil(2^32 / d) = (2^32 + e) / d with 0 <= e < d, q = umulhi(n, m).  Exact
+// while n * e < 2^32, i.e. for every n < 2^32 / d (n < 2^16 for any d < 2^16).
 struct FastDiv {
     uint32_t d, m;
     __host__ __device__ FastDiv() : d(1), m(0) {}

@@ -325,3 +325,30 @@ def test_truncate_rejects_cutting_a_committed_page():
     assert cache.seq_lens.tolist() == [40]
     with pytest.raises(RuntimeError, match="inconsistent"):
         cache.check()
+
+
+@pytest.mark.parametrize("kv", ["int8", "int4"])
+def test_append_rounds_half_integer_quotients_like_the_reference(kv):
+    """Codes of values whose quotient x / s is exactly a half-integer (ties go
+    away from zero, csrc/quantize.cu:51-57) or 2^-4 (INT8) / 2^-7 (INT4) beside
+    one: each page has absmax = qmax, so s = 1 and x / s = x.  The append forms
+    x / s as x * (1 / s) and must take the IEEE quotient at the ties."""
+    qmax = 127 if kv == "int8" else 7
+    B, H, D, P = 2, 2, 64, 16
+    step = 2.0 ** -4 if kv == "int8" else 2.0 ** -7  # fp16 spacing near the largest halves used
+    base = np.arange(-qmax, qmax) + 0.5  # every half-integer in range
+    vals = np.concatenate([base, base + step, base - step])
+    rng = np.random.default_rng(11)
+    k = rng.choice(vals, size=(B, P, H, D)).astype(np.float16)
+    v = rng.choice(vals, size=(B, P, H, D)).astype(np.float16)
+    k[:, 0, 0, 0] = qmax  # absmax of every page = qmax -> scale exactly 1
+    v[:, 0, 0, 0] = -qmax
+    cache = _cache_cls()(1, B, H, D, page_size=P, num_pages=8, max_blocks=4, kv_dtype=kv)
+    model = O.PagedCacheModel(B, 8, P, H, D, kv_dtype=kv, staging_dtype=np.float16, max_blocks=4)
+    cache.begin_step(P)
+    cache.append(0, torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda())
+    model.append(k, v)
+    torch.cuda.synchronize()
+    cache.check()
+    _assert_state_equal(cache, model)
+    assert all(model.k_scales[int(model.block_tables[b, 0])] == 1.0 for b in range(B))

@@ -1,0 +1,90 @@
+"""Both decode-attention kernels on the layouts either can serve.
+
+16-token pages with page scales and fp16 staged tails run the bulk-copy
+kernel for INT8 pools and the register-streaming kernel for INT4 pools by
+default (metagross_b200/csrc/mg_attention.cu, tma_applies); the environment
+variable METAGROSS_B200_ATTENTION forces one of them (``registers`` or
+``bulk``).  Each case here runs under both and is compared with the oracle's
+float64 dequantize-then-attend path (|out - ref| <= 2e-3 + 2^-11 |ref|), and
+the two kernels' outputs with each other.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _cache_cls():
+    from metagross_b200.batched import BatchedPagedKVCache
+
+    return BatchedPagedKVCache
+
+
+CASES = {
+    # name: (kv, B, hq, hkv, lens)
+    "int8_mha_tails": ("int8", 6, 12, 12, [1, 16, 17, 100, 255, 1023]),
+    "int8_gqa8": ("int8", 5, 32, 4, [128, 600, 16, 33, 1500]),
+    "int4_gqa8": ("int4", 5, 32, 4, [128, 600, 16, 33, 1500]),
+    "int4_mha": ("int4", 4, 8, 8, [5, 64, 300, 901]),
+    "int8_group16": ("int8", 3, 32, 2, [40, 700, 1200]),
+}
+
+
+def _build(kv, B, hq, hkv, lens, seed):
+    P, D = 16, 64
+    g = torch.Generator().manual_seed(seed)
+    mb = max(lens) // P + 2
+    cache = _cache_cls()(1, B, hkv, D, page_size=P, num_pages=B * mb, max_blocks=mb, kv_dtype=kv)
+    model = O.PagedCacheModel(B, B * mb, P, hkv, D, kv_dtype=kv, staging_dtype=np.float16, max_blocks=mb)
+    T = max(lens)
+    k = torch.randn(B, T, hkv, D, generator=g)
+    v = torch.randn(B, T, hkv, D, generator=g)
+    k[torch.rand(k.shape, generator=g) < 0.01] *= 8
+    k, v = k.half(), v.half()
+    n = torch.tensor(lens, dtype=torch.int32)
+    cache.begin_step(n)
+    cache.append(0, k.cuda(), v.cuda())
+    model.append(k.numpy(), v.numpy(), n.numpy())
+    q = torch.randn(B, hq, D, generator=g).half()
+    return cache, model, q
+
+
+@pytest.mark.parametrize("case", sorted(CASES))
+def test_both_kernels_match_the_oracle_and_each_other(case, monkeypatch):
+    kv, B, hq, hkv, lens = CASES[case]
+    cache, model, q = _build(kv, B, hq, hkv, lens, seed=sum(map(ord, case)))
+    ref = model.attend(q.float().numpy(), 1.0 / 8)
+    outs = {}
+    for path in ("registers", "bulk"):
+        monkeypatch.setenv("METAGROSS_B200_ATTENTION", path)
+        cache.invalidate_plan()
+        out = cache.attend(0, q.cuda())
+        torch.cuda.synchronize()
+        cache.check()
+        o = out.float().cpu().numpy()
+        err = float((np.abs(o - ref) - np.abs(ref) * 2.0 ** -11).max())
+        assert err < 2e-3, (path, err)
+        outs[path] = o
+    assert np.abs(outs["registers"] - outs["bulk"]).max() < 4e-3
+
+
+def test_bulk_kernel_stream_k_int8():
+    """More non-empty sequences than SMs on the bulk-copy kernel (INT8): CTAs
+    hold several segments, and cut sequences merge through the tickets."""
+    rng = np.random.default_rng(7)
+    B = 200
+    lens = np.maximum(1, np.exp(rng.normal(np.log(300), 1.0, B)).round().astype(int)).clip(max=3000).tolist()
+    lens[3] = 0
+    cache, model, q = _build("int8", B, 12, 12, lens, seed=9)
+    out = cache.attend(0, q.cuda())
+    torch.cuda.synchronize()
+    cache.check()
+    assert int(cache._plan.view(torch.int32)[5].item()) == 2  # stream-K
+    ref = model.attend(q.float().numpy(), 1.0 / 8)
+    o = out.float().cpu().numpy()
+    assert np.all(o[3] == 0.0)
+    err = float((np.abs(o - ref) - np.abs(ref) * 2.0 ** -11).max())
+    assert err < 2e-3, err
