@@ -496,11 +496,17 @@ def reference_cuda_leg(cache, w, q, sample_steps=3):
         return {"unavailable": "reference not installed in baseline/_ref"}
     if w["kv"] != "int8" or w["d"] != 64:
         return {"unavailable": "the reference's committed-page attention is INT8 with head_dim 64 only"}
-    sys.path.insert(0, ref_dir)
-    try:
-        from metagross import _C as ref_C
-    finally:
-        sys.path.remove(ref_dir)
+    # loaded by file path under a private name: this repository's own
+    # ``metagross`` package (the drop-in alias) must not shadow it, nor it that
+    import glob
+    import importlib.util
+
+    so = sorted(glob.glob(os.path.join(ref_dir, "metagross", "_C*.so")))
+    if not so:
+        return {"unavailable": "reference _C extension missing from baseline/_ref"}
+    spec = importlib.util.spec_from_file_location("metagross_reference_build._C", so[0])
+    ref_C = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref_C)
     L, B, P = cache.num_layers, cache.batch, cache.page_size
     lens = cache.seq_lens.cpu().tolist()
     tables = [cache.block_tables[b, : lens[b] // P].contiguous() for b in range(B)]
