@@ -444,6 +444,24 @@ def gather_bench(device, workload="tinyllama_int4", reps=20):
             "bytes_per_launch": int(byts)}
 
 
+def reference_decode(sequences=2, new_tokens=64, prompt_len=128):
+    """The reference's generate_tinyllama_fused on the same architecture
+    (baseline/time_reference_decode.py), in a child interpreter whose import
+    path holds only the reference install."""
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    script = os.path.join(ROOT, "baseline", "time_reference_decode.py")
+    if not os.path.isdir(os.path.join(ref_dir, "metagross")):
+        return {"unavailable": "reference not installed in baseline/_ref"}
+    env = dict(os.environ, PYTHONPATH=ref_dir)
+    r = subprocess.run([sys.executable, script, "--sequences", str(sequences), "--new-tokens", str(new_tokens),
+                        "--prompt-len", str(prompt_len)], cwd=os.path.join(ROOT, "baseline"), env=env,
+                       capture_output=True, text=True, timeout=1200)
+    for line in r.stdout.splitlines():
+        if line.startswith("{"):
+            return json.loads(line)
+    return {"unavailable": f"reference decode failed (rc {r.returncode}): {r.stderr.strip().splitlines()[-1:]}"}
+
+
 def decode_model(device, batch=64, prompt_len=128, new_tokens=256, kv="int8"):
     """End-to-end greedy decode of the TinyLlama-1.1B architecture (22 layers,
     hidden 2048, 32 q / 4 kv heads, FFN 5632, vocab 32000, rotary, fp16) with
@@ -796,8 +814,13 @@ def main():
         print(json.dumps(gather_bench(torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))), args.workload)))
         return
     if args.decode_model:
-        print(json.dumps(decode_model(torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))),
-                                      new_tokens=args.new_tokens)))
+        line = decode_model(torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))), new_tokens=args.new_tokens)
+        if not args.no_reference_cuda:
+            ref = reference_decode()
+            line["reference_decode"] = ref
+            if "value" in ref:
+                line["speedup_vs_reference_decode"] = round(line["value"] / ref["value"], 1)
+        print(json.dumps(line))
         return
     if args.append_sweep:
         print(json.dumps(append_sweep(torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))),

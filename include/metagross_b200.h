@@ -206,6 +206,24 @@ MG_API mg_status mg_kv_append(const mg_cache_layout* layout, const mg_layer_ptrs
                        int32_t batch, const void* k_new, const void* v_new, int32_t new_dtype,
                        int32_t max_new, int32_t* dev_status, mg_stream_t stream);
 
+/* mg_kv_append for a Llama-style decode or prefill step whose new tokens come
+ * straight from the fused q|k|v projection: qkv fp16 [batch, max_new,
+ * (num_q_heads + 2 Hkv) * D] (q heads, then k heads, then v heads, as
+ * mg_rope_qkv_f16 takes them).  K is rotated (rotate-half rotary embedding at
+ * position seq_len_before + t, tables cos/sin [table_rows, D / 2] fp32,
+ * products rounded separately, the result rounded to fp16) on its way into
+ * staging or a committed page, V is appended as it is, and the rotated q of
+ * every new token is written to q_out [batch, max_new, num_q_heads, D] fp16 --
+ * one launch where mg_rope_qkv_f16 + mg_kv_append take two, with identical
+ * results.  fp16 staging only; a position beyond the table sets
+ * MG_DEV_BAD_ARGUMENT.  Replaces the rotary embedding + per-layer append of
+ * metagross/generate_llama.py:20-37,103-106 for a batch. */
+MG_API mg_status mg_kv_append_rope(const mg_cache_layout* layout, const mg_layer_ptrs* layer,
+                            const int32_t* block_tables, const int32_t* seq_lens, const int32_t* n_new,
+                            int32_t batch, const void* qkv, int32_t num_q_heads, const float* cos_table,
+                            const float* sin_table, int32_t table_rows, void* q_out, int32_t max_new,
+                            int32_t* dev_status, mg_stream_t stream);
+
 /* Fused paged decode attention for a batch: committed quantized pages through
  * the block table plus the exact staged tail, one online softmax, split over
  * the context with an in-kernel merge.  q [batch, num_q_heads, D] (q_dtype),

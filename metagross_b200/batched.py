@@ -135,6 +135,20 @@ class BatchedPagedKVCache:
                            self.staging_k[layer], self.staging_v[layer], self.block_tables, self.seq_lens,
                            self.n_new, k_new, v_new, self.status)
 
+    def append_rope(self, layer: int, qkv: torch.Tensor, num_q_heads: int, cos: torch.Tensor, sin: torch.Tensor,
+                    q_out: torch.Tensor) -> None:
+        """``append`` for a step whose tokens come straight from a fused q|k|v
+        projection, qkv fp16 [B, T, (num_q_heads + 2 Hkv) * D]: K is rotated
+        (rotate-half, at each token's position = cached length before it) as it
+        is written, V as it is, and the rotated q goes to q_out (B * T *
+        num_q_heads * D fp16 elements) -- one launch (mg_kv_append_rope).
+        cos / sin: fp32 [positions, D / 2]."""
+        if qkv.dim() == 2:
+            qkv = qkv.unsqueeze(1)
+        _get_C().kv_append_rope(self.k_pool[layer], self.v_pool[layer], self.k_scales[layer], self.v_scales[layer],
+                                self.staging_k[layer], self.staging_v[layer], self.block_tables, self.seq_lens,
+                                self.n_new, qkv, num_q_heads, cos, sin, q_out, self.status)
+
     def invalidate_plan(self) -> None:
         """Mark the decode plan stale (after writing seq_lens or block_tables directly)."""
         self._plan_ok = False

@@ -386,6 +386,37 @@ void kv_append(torch::Tensor k_pool, torch::Tensor v_pool, torch::Tensor k_scale
                  "kv_append");
 }
 
+void kv_append_rope(torch::Tensor k_pool, torch::Tensor v_pool, torch::Tensor k_scales, torch::Tensor v_scales,
+                    torch::Tensor staging_k, torch::Tensor staging_v, torch::Tensor block_tables,
+                    torch::Tensor seq_lens, torch::Tensor n_new, torch::Tensor qkv, int64_t num_q_heads,
+                    torch::Tensor cos_table, torch::Tensor sin_table, torch::Tensor q_out,
+                    c10::optional<torch::Tensor> status) {
+    const c10::cuda::CUDAGuard guard(k_pool.device());
+    auto p = make_pools(k_pool, v_pool, k_scales, v_scales, staging_k, staging_v, block_tables);
+    const int64_t B = block_tables.size(0);
+    check_i32_vec(seq_lens, B, "seq_lens");
+    check_i32_vec(n_new, B, "n_new");
+    const int64_t D = p.L.head_dim, hkv = p.L.num_kv_heads;
+    TORCH_CHECK(qkv.is_cuda() && qkv.scalar_type() == torch::kHalf && qkv.dim() == 3 && qkv.size(0) == B &&
+                    qkv.size(2) == (num_q_heads + 2 * hkv) * D && qkv.is_contiguous(),
+                "qkv must be a contiguous fp16 CUDA tensor [batch, max_new, (num_q_heads + 2 num_kv_heads) * head_dim]");
+    TORCH_CHECK(cos_table.is_cuda() && sin_table.is_cuda() && cos_table.scalar_type() == torch::kFloat32 &&
+                    sin_table.scalar_type() == torch::kFloat32 && cos_table.dim() == 2 &&
+                    cos_table.sizes() == sin_table.sizes() && cos_table.size(1) == D / 2 &&
+                    cos_table.is_contiguous() && sin_table.is_contiguous(),
+                "cos/sin tables must be contiguous fp32 CUDA tensors [positions, head_dim / 2]");
+    TORCH_CHECK(q_out.is_cuda() && q_out.scalar_type() == torch::kHalf && q_out.is_contiguous() &&
+                    q_out.numel() == B * qkv.size(1) * num_q_heads * D,
+                "q_out must be a contiguous fp16 CUDA tensor of batch x max_new x num_q_heads x head_dim elements");
+    check_status(mg_kv_append_rope(&p.L, &p.ptrs, block_tables.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(),
+                                   n_new.data_ptr<int32_t>(), static_cast<int32_t>(B), qkv.data_ptr(),
+                                   static_cast<int32_t>(num_q_heads), cos_table.data_ptr<float>(),
+                                   sin_table.data_ptr<float>(), static_cast<int32_t>(cos_table.size(0)),
+                                   q_out.data_ptr(), static_cast<int32_t>(qkv.size(1)), status_ptr(status),
+                                   cur_stream()),
+                 "kv_append_rope");
+}
+
 void truncate_sequences(torch::Tensor free_stack, torch::Tensor n_free, torch::Tensor in_use,
                         torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor seq_ids,
                         torch::Tensor new_lens, int64_t page_size, c10::optional<torch::Tensor> status) {
@@ -632,6 +663,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           pybind11::arg("out_k"), pybind11::arg("out_v"), pybind11::arg("status") = pybind11::none());
     m.def("rmsnorm", &rmsnorm, "RMSNorm over the last dimension (fp16, fp32 math)", pybind11::arg("x"),
           pybind11::arg("w"), pybind11::arg("eps"));
+    m.def("kv_append_rope", &kv_append_rope,
+          "kv_append with the rotary embedding of K fused in, reading K / V from a q|k|v projection and writing "
+          "the rotated q",
+          pybind11::arg("k_pool"), pybind11::arg("v_pool"), pybind11::arg("k_scales"), pybind11::arg("v_scales"),
+          pybind11::arg("staging_k"), pybind11::arg("staging_v"), pybind11::arg("block_tables"),
+          pybind11::arg("seq_lens"), pybind11::arg("n_new"), pybind11::arg("qkv"), pybind11::arg("num_q_heads"),
+          pybind11::arg("cos_table"), pybind11::arg("sin_table"), pybind11::arg("q_out"),
+          pybind11::arg("status") = pybind11::none());
     m.def("rope_qkv", &rope_qkv, "Split q | k | v, rotary embedding of q and k at per-row positions",
           pybind11::arg("qkv"), pybind11::arg("pos"), pybind11::arg("cos_table"), pybind11::arg("sin_table"),
           pybind11::arg("q"), pybind11::arg("k"), pybind11::arg("v"));

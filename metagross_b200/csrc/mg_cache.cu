@@ -290,7 +290,24 @@ struct AppendParams {
     int32_t scale_th;  // scales [N, P, Hkv] (one per token and head) instead of [N]
     int64_t num_pages;
     int32_t* status;
+    int64_t new_stride;     // elements from one new token's row to the next (row, or (Hq + 2 Hkv) D in a qkv buffer)
+    const float* rope_cos;  // non-null: rotate K (and q) by these tables [rope_rows, D / 2] (rotate-half)
+    const float* rope_sin;
+    int32_t rope_rows;
+    int32_t Hq;
+    const __half* q_src;  // q heads of the new tokens, row stride new_stride
+    __half* q_out;        // [batch, max_new, Hq, D] rotated q
 };
+
+// Rotate-half rotary embedding of one element pair at position pos (fp32
+// products, one rounding to fp16 each, as the reference's rotary embedding of
+// fp16 activations): (x1, x2) -> (x1 c - x2 s, x2 c + x1 s); own / partner are
+// this element and the one D/2 away, lower says which half this one is in.
+__device__ __forceinline__ float rope_elem(float own, float partner, float c, float s, bool lower) {
+    const float r = lower ? __fsub_rn(__fmul_rn(own, c), __fmul_rn(partner, s))
+                          : __fadd_rn(__fmul_rn(own, c), __fmul_rn(partner, s));
+    return __half2float(__float2half_rn(r));
+}
 
 // Code of 8 consecutive elements into the pool at element e of a page (INT8:
 // 8 bytes, INT4: 4 bytes of nibbles, the even element in the low nibble),
@@ -332,22 +349,68 @@ __global__ void __launch_bounds__(kAppendThreads, KEEP <= 2 ? 4 : 2) kv_append_k
         return;
     }
     const int old = new_len - add;
+    if (kv == 2) {
+        // rotary q of this sequence's new tokens (the rotary variant's third grid slice)
+        if (jj != 0) return;
+        const int half = p.D / 2;
+        const int64_t npairs = static_cast<int64_t>(add) * p.Hq * half;
+        for (int64_t i = threadIdx.x; i < npairs; i += blockDim.x) {
+            const int64_t th = i / half;  // (token, head)
+            const int jd = static_cast<int>(i - th * half);
+            const int t = static_cast<int>(th / p.Hq), h = static_cast<int>(th - static_cast<int64_t>(t) * p.Hq);
+            const int pos = old + t;
+            if (pos >= p.rope_rows) {
+                flag(p.status, MG_DEV_BAD_ARGUMENT);
+                continue;
+            }
+            const __half* src = p.q_src + (static_cast<int64_t>(b) * p.max_new + t) * p.new_stride + h * p.D;
+            const float c = p.rope_cos[static_cast<int64_t>(pos) * half + jd];
+            const float sn = p.rope_sin[static_cast<int64_t>(pos) * half + jd];
+            const float x1 = __half2float(src[jd]), x2 = __half2float(src[jd + half]);
+            __half* dst = p.q_out + ((static_cast<int64_t>(b) * p.max_new + t) * p.Hq + h) * p.D;
+            dst[jd] = __float2half_rn(rope_elem(x1, x2, c, sn, true));
+            dst[jd + half] = __float2half_rn(rope_elem(x2, x1, c, sn, false));
+        }
+        return;
+    }
     const int P = p.P, row = p.row;
     const int j0 = old / P, jlast = (new_len - 1) / P;
     const int j = j0 + jj;
     if (j > jlast) return;
     const int64_t pe = static_cast<int64_t>(P) * row;  // elements per page
     ST* staging = static_cast<ST*>(kv ? p.staging_v : p.staging_k) + static_cast<int64_t>(b) * pe;
-    const NT* src_new = static_cast<const NT*>(kv ? p.v_new : p.k_new) + static_cast<int64_t>(b) * p.max_new * row;
+    const NT* src_new =
+        static_cast<const NT*>(kv ? p.v_new : p.k_new) + static_cast<int64_t>(b) * p.max_new * p.new_stride;
     const int page_start = j * P;
 
+    // 8 consecutive elements at element c of new token t (step-relative); K
+    // rotated at position old + t when the call carries rotary tables
+    auto load_new8 = [&](int t, int64_t c, float (&v)[8]) {
+        const NT* src = src_new + static_cast<int64_t>(t) * p.new_stride;
+        Vec8<NT>::load(src + c, v);
+        if (p.rope_cos != nullptr && kv == 0) {
+            const int half = p.D / 2;
+            const int d = static_cast<int>(c - (c / p.D) * p.D);
+            const bool lower = d < half;
+            float w[8];
+            Vec8<NT>::load(src + c + (lower ? half : -half), w);
+            int pos = old + t;
+            if (pos >= p.rope_rows) {
+                flag(p.status, MG_DEV_BAD_ARGUMENT);
+                pos = 0;
+            }
+            const int64_t ti = static_cast<int64_t>(pos) * half + (lower ? d : d - half);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = rope_elem(v[i], w[i], p.rope_cos[ti + i], p.rope_sin[ti + i], lower);
+        }
+    };
     // 8 consecutive elements at element e of page j: staged rows, then this step's tokens
     auto load8 = [&](int64_t e, float (&v)[8]) {
         const int t = static_cast<int>(e / row);
         const int tok = page_start + t;
         const int64_t c = e - static_cast<int64_t>(t) * row;
         if (tok < old) Vec8<ST>::load(staging + static_cast<int64_t>(t) * row + c, v);
-        else Vec8<NT>::load(src_new + static_cast<int64_t>(tok - old) * row + c, v);
+        else load_new8(tok - old, c, v);
     };
     if (page_start + P <= new_len) {  // page j fills during this step: commit it
         const int32_t page = j < p.max_blocks ? p.block_tables[static_cast<int64_t>(b) * p.max_blocks + j] : -1;
@@ -443,7 +506,7 @@ __global__ void __launch_bounds__(kAppendThreads, KEEP <= 2 ? 4 : 2) kv_append_k
             const int t = static_cast<int>(e / row);
             const int64_t c = e - static_cast<int64_t>(t) * row;
             float v[8];
-            Vec8<NT>::load(src_new + static_cast<int64_t>(jlast * P + t - old) * row + c, v);
+            load_new8(jlast * P + t - old, c, v);
             Vec8<ST>::store(staging + e, v);
         }
     }
@@ -604,10 +667,18 @@ extern "C" mg_status mg_free_sequences(const mg_allocator* a, const int32_t* blo
                                  page_size, dev_status, stream);
 }
 
-extern "C" mg_status mg_kv_append(const mg_cache_layout* L, const mg_layer_ptrs* lp, const int32_t* block_tables,
-                                  const int32_t* seq_lens, const int32_t* n_new, int32_t batch, const void* k_new,
-                                  const void* v_new, int32_t new_dtype, int32_t max_new, int32_t* dev_status,
-                                  mg_stream_t stream) {
+namespace mg {
+namespace {
+
+// The append proper: checks, parameters and the launch.  new_stride: elements
+// between consecutive new-token rows (row for k_new / v_new tensors).  With
+// rotary tables (fp16 tokens and staging only) K is rotated on the way in and
+// a third grid slice writes the rotated q of q_src to q_out.
+mg_status append_launch(const mg_cache_layout* L, const mg_layer_ptrs* lp, const int32_t* block_tables,
+                        const int32_t* seq_lens, const int32_t* n_new, int32_t batch, const void* k_new,
+                        const void* v_new, int32_t new_dtype, int32_t max_new, int64_t new_stride,
+                        const float* rope_cos, const float* rope_sin, int32_t rope_rows, int32_t num_q_heads,
+                        const void* q_src, void* q_out, int32_t* dev_status, mg_stream_t stream) {
     mg_status st = check_layout(L);
     if (st != MG_OK) return st;
     MG_REQUIRE(lp != nullptr, "null layer pointers");
@@ -622,6 +693,9 @@ extern "C" mg_status mg_kv_append(const mg_cache_layout* L, const mg_layer_ptrs*
     MG_REQUIRE(aligned16(k_new) && aligned16(v_new) && aligned16(lp->staging_k) && aligned16(lp->staging_v) &&
                    aligned16(lp->k_pool) && aligned16(lp->v_pool),
                "k_new, v_new, staging and pools must be 16-byte aligned");
+    const int64_t row = static_cast<int64_t>(L->num_kv_heads) * L->head_dim;
+    MG_REQUIRE(new_stride >= row && new_stride % 8 == 0, "new-token row stride must be >= %lld and a multiple of 8",
+               (long long)row);
     AppendParams p;
     p.k_new = k_new;
     p.v_new = v_new;
@@ -637,17 +711,24 @@ extern "C" mg_status mg_kv_append(const mg_cache_layout* L, const mg_layer_ptrs*
     p.seq_lens = seq_lens;
     p.n_new = n_new;
     p.P = L->page_size;
-    p.row = L->num_kv_heads * L->head_dim;
+    p.row = static_cast<int32_t>(row);
     p.D = L->head_dim;
     p.scale_th = L->scale_layout == MG_SCALE_TOKEN_HEAD;
     p.num_pages = L->num_pages;
     p.status = dev_status;
+    p.new_stride = new_stride;
+    p.rope_cos = rope_cos;
+    p.rope_sin = rope_sin;
+    p.rope_rows = rope_rows;
+    p.Hq = num_q_heads;
+    p.q_src = static_cast<const __half*>(q_src);
+    p.q_out = static_cast<__half*>(q_out);
     const int64_t touch = (static_cast<int64_t>(max_new) + L->page_size - 1) / L->page_size + 1;
     MG_REQUIRE(touch <= 65535,
                "max_new %d spans %lld pages of %d tokens; one append takes at most 65534 pages per sequence "
                "(split the prefill into several steps)",
                max_new, (long long)touch - 1, L->page_size);
-    dim3 grid(batch, static_cast<unsigned>(touch), 2);
+    dim3 grid(batch, static_cast<unsigned>(touch), rope_cos ? 3 : 2);
     const bool i4 = L->kv_dtype == MG_KV_INT4;
     const bool s16 = L->staging_dtype == MG_F16, n16 = new_dtype == MG_F16;
     cudaStream_t s = as_stream(stream);
@@ -664,6 +745,36 @@ extern "C" mg_status mg_kv_append(const mg_cache_layout* L, const mg_layer_ptrs*
     if (small) go(std::integral_constant<int, 2>{});
     else go(std::integral_constant<int, 8>{});
     return check_launch("kv_append_kernel");
+}
+
+}  // namespace
+}  // namespace mg
+
+extern "C" mg_status mg_kv_append(const mg_cache_layout* L, const mg_layer_ptrs* lp, const int32_t* block_tables,
+                                  const int32_t* seq_lens, const int32_t* n_new, int32_t batch, const void* k_new,
+                                  const void* v_new, int32_t new_dtype, int32_t max_new, int32_t* dev_status,
+                                  mg_stream_t stream) {
+    const int64_t row = L ? static_cast<int64_t>(L->num_kv_heads) * L->head_dim : 0;
+    return mg::append_launch(L, lp, block_tables, seq_lens, n_new, batch, k_new, v_new, new_dtype, max_new, row,
+                             nullptr, nullptr, 0, 0, nullptr, nullptr, dev_status, stream);
+}
+
+extern "C" mg_status mg_kv_append_rope(const mg_cache_layout* L, const mg_layer_ptrs* lp,
+                                       const int32_t* block_tables, const int32_t* seq_lens, const int32_t* n_new,
+                                       int32_t batch, const void* qkv, int32_t num_q_heads, const float* cos_table,
+                                       const float* sin_table, int32_t table_rows, void* q_out, int32_t max_new,
+                                       int32_t* dev_status, mg_stream_t stream) {
+    MG_REQUIRE(L != nullptr, "null layout");
+    MG_REQUIRE(L->staging_dtype == MG_F16, "the rotary append takes fp16 tokens into fp16 staging");
+    MG_REQUIRE(num_q_heads >= 1 && L->head_dim % 16 == 0, "num_q_heads must be positive and head_dim % 16 == 0");
+    MG_REQUIRE(qkv && cos_table && sin_table && q_out && table_rows >= 1, "null pointer or empty rotary table");
+    MG_REQUIRE(aligned16(q_out), "q_out must be 16-byte aligned");
+    const int64_t D = L->head_dim, hkv = L->num_kv_heads;
+    const int64_t stride = (num_q_heads + 2 * hkv) * D;
+    const __half* base = static_cast<const __half*>(qkv);
+    return mg::append_launch(L, lp, block_tables, seq_lens, n_new, batch, base + num_q_heads * D,
+                             base + (num_q_heads + hkv) * D, MG_F16, max_new, stride, cos_table, sin_table,
+                             table_rows, num_q_heads, qkv, q_out, dev_status, stream);
 }
 
 extern "C" mg_status mg_gather_dequant(const mg_cache_layout* L, const mg_layer_ptrs* lp, const int32_t* block_tables,

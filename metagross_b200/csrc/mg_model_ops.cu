@@ -107,8 +107,9 @@ __global__ void __launch_bounds__(kOpThreads) rope_qkv_kernel(const __half* qkv,
         const float c = cosb[p * half + j], s = sinb[p * half + j];
         const float x1 = __half2float(src[j]), x2 = __half2float(src[j + half]);
         __half* dst = h < Hq ? q + (static_cast<int64_t>(b) * Hq + h) * D : k + (static_cast<int64_t>(b) * Hkv + h - Hq) * D;
-        dst[j] = __float2half(x1 * c - x2 * s);
-        dst[j + half] = __float2half(x2 * c + x1 * s);
+        // products rounded separately (no FMA contraction), as mg_kv_append_rope does
+        dst[j] = __float2half_rn(__fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s)));
+        dst[j + half] = __float2half_rn(__fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s)));
     } else if (i < nrot + nv) {
         const int64_t e = i - nrot;
         const int64_t b = e / (static_cast<int64_t>(Hkv) * D);

@@ -51,7 +51,8 @@ class LlamaDecoder:
     """
 
     def __init__(self, shape: LlamaShape, batch: int, max_len: int, kv_dtype: str = "int8", page_size: int = 16,
-                 device="cuda", seed: int = 0, weights: dict | None = None, keep_logits: bool = False):
+                 device="cuda", seed: int = 0, weights: dict | None = None, keep_logits: bool = False,
+                 fused_rope: bool = True):
         self.s = shape
         self.batch, self.max_len = batch, max_len
         self.device = torch.device(device)
@@ -88,6 +89,9 @@ class LlamaDecoder:
         # the last step's logits, kept only on request (tests)
         self.logits = torch.empty(batch, shape.vocab, dtype=dt, device=self.device) if keep_logits else None
         self.graph = None
+        # rotary embedding inside the KV append (one launch per layer) or as its
+        # own launch before a plain append (the same results)
+        self.fused_rope = fused_rope
 
     # ------------------------------------------------- torch restatement of the pieces
     # (the decode step below runs the fused kernels; these are the plain torch
@@ -147,7 +151,7 @@ class LlamaDecoder:
         c.begin_step(T)
         for i in range(s.layers):
             qkv = self._norm(x, self.w[f"{i}.n1"]) @ self.w[f"{i}.wqkv"]
-            C.rope_qkv(qkv, pos, self.cos, self.sin, q, k, v)
+            C.rope_qkv(qkv, pos, self.cos, self.sin, q, k, v)  # k and v also feed the prompt's own attention
             c.append(i, k.view(B, T, s.kv_heads, D), v.view(B, T, s.kv_heads, D))
             o = F.scaled_dot_product_attention(q.view(B, T, s.heads, D).transpose(1, 2),
                                                k.view(B, T, s.kv_heads, D).transpose(1, 2),
@@ -164,15 +168,19 @@ class LlamaDecoder:
     # ---------------------------------------------------------------- decode
     def _step(self):
         """One token for every sequence: self.ids at positions self.pos -> self.ids.
-        Per layer: RMSNorm, the qkv GEMM, rotary + split (one kernel), append,
-        paged attention, the o-projection GEMM accumulated into x, then the MLP."""
+        Per layer: RMSNorm, the qkv GEMM, the KV append with the rotary
+        embedding fused in (it also writes the rotated q), paged attention, the
+        o-projection GEMM accumulated into x, then the MLP."""
         c, C = self.cache, _get_C()
         x = self.w["embed"][self.ids]
         c.begin_step(1)
         for i in range(self.s.layers):
             qkv = self._norm(x, self.w[f"{i}.n1"]) @ self.w[f"{i}.wqkv"]
-            C.rope_qkv(qkv, self.pos, self.cos, self.sin, self.qb, self.kb, self.vb)
-            c.append(i, self.kb, self.vb)
+            if self.fused_rope:
+                c.append_rope(i, qkv, self.s.heads, self.cos, self.sin, self.qb)
+            else:
+                C.rope_qkv(qkv, self.pos, self.cos, self.sin, self.qb, self.kb, self.vb)
+                c.append(i, self.kb, self.vb)
             o = c.attend(i, self.qb, out=self.attn_out, max_context=c.max_blocks * c.page_size)
             x.addmm_(o.view(self.batch, -1), self.w[f"{i}.wo"])
             self._ffn(i, x)

@@ -106,3 +106,71 @@ def test_fused_dense_ops_match_torch():
     assert (q.float() - rot(qq, Hq).float()).abs().max().item() <= 2e-3
     assert (k.float() - rot(kk, Hkv).float()).abs().max().item() <= 2e-3
     assert torch.equal(v, vv.reshape(B, Hkv, D))
+
+
+@pytest.mark.parametrize("kv", ["int8", "int4"])
+def test_fused_rotary_append_equals_rotary_then_append(kv):
+    """mg_kv_append_rope against mg_rope_qkv_f16 + mg_kv_append on twin caches:
+    pools, scales, staging and block tables bit for bit, and the same rotated
+    q, over a prefill-sized step (page commits) and decode steps."""
+    from metagross_b200 import _C
+    from metagross_b200.batched import BatchedPagedKVCache
+
+    B, Hq, Hkv, D, P = 3, 8, 2, 64, 16
+    g = torch.Generator(device="cuda").manual_seed(21)
+    ang = torch.outer(torch.arange(128, device="cuda").float(),
+                      1.0 / 10000 ** (torch.arange(0, D, 2, device="cuda").float() / D))
+    cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+    mk = lambda: BatchedPagedKVCache(1, B, Hkv, D, page_size=P, num_pages=32, max_blocks=8, kv_dtype=kv)  # noqa: E731
+    fused, plain = mk(), mk()
+    for T in (37, 1, 1, 5, 1):
+        n = torch.randint(0, T + 1, (B,), generator=torch.Generator().manual_seed(T), dtype=torch.int32)
+        qkv = torch.randn(B, T, (Hq + 2 * Hkv) * D, generator=g, device="cuda").half()
+        lens = fused.seq_lens.long()
+        pos = (lens[:, None] + torch.arange(T, device="cuda")[None]).reshape(-1)
+        q_plain = torch.empty(B * T, Hq, D, device="cuda").half()
+        k_plain = torch.empty(B * T, Hkv, D, device="cuda").half()
+        v_plain = torch.empty_like(k_plain)
+        _C.rope_qkv(qkv.reshape(B * T, -1), pos, cos, sin, q_plain, k_plain, v_plain)
+        for c in (fused, plain):
+            c.begin_step(n)
+        q_fused = torch.zeros(B, T, Hq, D, device="cuda").half()
+        fused.append_rope(0, qkv, Hq, cos, sin, q_fused)
+        plain.append(0, k_plain.view(B, T, Hkv, D), v_plain.view(B, T, Hkv, D))
+        torch.cuda.synchronize()
+        fused.check()
+        plain.check()
+        for name in ("k_pool", "v_pool", "k_scales", "v_scales", "staging_k", "staging_v", "block_tables",
+                     "seq_lens"):
+            assert torch.equal(getattr(fused, name), getattr(plain, name)), (T, name)
+        qp = q_plain.view(B, T, Hq, D)
+        for b in range(B):
+            assert torch.equal(q_fused[b, :int(n[b])], qp[b, :int(n[b])]), (T, b)
+
+
+def test_fused_rotary_decoder_equals_unfused():
+    from metagross_b200.llama import LlamaDecoder, LlamaShape
+
+    p = _prompt().cuda()
+    toks = []
+    for fused in (True, False):
+        d = LlamaDecoder(LlamaShape(**SHAPE), batch=3, max_len=64, kv_dtype="int8", seed=5, fused_rope=fused)
+        d.prefill(p)
+        d.capture()
+        toks.append(d.decode(16))
+        d.cache.check()
+    assert torch.equal(toks[0], toks[1])
+
+
+def test_fused_rotary_append_flags_a_position_beyond_the_table():
+    from metagross_b200.batched import BatchedPagedKVCache
+
+    B, Hq, Hkv, D = 2, 4, 2, 64
+    c = BatchedPagedKVCache(1, B, Hkv, D, page_size=16, num_pages=8, max_blocks=4)
+    cos = torch.ones(4, D // 2, device="cuda")
+    sin = torch.zeros(4, D // 2, device="cuda")
+    qkv = torch.randn(B, 6, (Hq + 2 * Hkv) * D, device="cuda").half()
+    c.begin_step(6)  # positions 0..5, the table has 4 rows
+    c.append_rope(0, qkv, Hq, cos, sin, torch.empty(B, 6, Hq, D, device="cuda").half())
+    torch.cuda.synchronize()
+    assert int(c.status.item()) & 0x80
