@@ -893,8 +893,11 @@ def main():
         L = m["L"]
         achieved = m["att_bytes_per_launch"] / (m["att_avg_ms"] / 1e3) / 1e9
         seq_steps = m["tot_batch"] * args.steps / (m["ms"] / 1e3)
-        kernel = "paged_decode_tma_kernel" if os.environ.get("METAGROSS_B200_ATTENTION") != "registers" \
-            else "paged_decode_kernel"
+        # which attention kernel ran: every workload here has 16-token pages, page scales, fp16 staging and
+        # head_dim 64, so the pool's code width decides (the rule of tma_applies in csrc/mg_attention.cu)
+        force = os.environ.get("METAGROSS_B200_ATTENTION", "")
+        bulk = force == "bulk" or (force != "registers" and w["kv"] == "int8")
+        kernel = "paged_decode_tma_kernel" if bulk else "paged_decode_kernel"
         line = {
             "metric": metric, "value": round(m["value"], 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": m["ms"] / args.steps, "higher_is_better": True,

@@ -217,7 +217,7 @@ MG_API mg_status mg_kv_append(const mg_cache_layout* layout, const mg_layer_ptrs
  * one launch where mg_rope_qkv_f16 + mg_kv_append take two, with identical
  * results.  fp16 staging only; a position beyond the table sets
  * MG_DEV_BAD_ARGUMENT.  Replaces the rotary embedding + per-layer append of
- * metagross/generate_llama.py:20-37,103-106 for a batch. */
+ * metagross/generate_llama.py:20-37,104-107 for a batch. */
 MG_API mg_status mg_kv_append_rope(const mg_cache_layout* layout, const mg_layer_ptrs* layer,
                             const int32_t* block_tables, const int32_t* seq_lens, const int32_t* n_new,
                             int32_t batch, const void* qkv, int32_t num_q_heads, const float* cos_table,

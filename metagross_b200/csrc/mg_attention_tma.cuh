@@ -142,7 +142,7 @@ __device__ __forceinline__ void regs_ready(const uint32_t* r, int n) {
 // Tiled TMA copy of one whole page into a stage: the permuted 4-D map
 // (row bytes, token, kv head, page) at (0, 0, 0, pid), or, when the driver
 // declined that map, one 3-D copy (row bytes, kv head, token of the pool) per
-// kv head issued by lanes 0 .. Hkv-1.  No multicast.
+// kv head issued by lanes 0 .. Hkv-1.  Every copy lands in this CTA's own shared memory.
 __device__ __forceinline__ void tma_page(uint8_t* dst, const CUtensorMap* tm, int pid, uint64_t* bar, int per_head,
                                          int Hkv, int P, int tile, int lane) {
     if (!per_head) {
