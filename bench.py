@@ -797,6 +797,9 @@ def main():
     ap.add_argument("--layers", type=int, default=None,
                     help="override the workload's layer count (a small case for profiling; the default run uses "
                          "the workload's own depth)")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the workload's sequence count (e.g. lognormal_int4 with 128 sequences is one "
+                         "rank's share of the 1024 at 8 GPUs)")
     ap.add_argument("--append-sweep", action="store_true",
                     help="instead of the decode benchmark, print the KV-append bandwidth sweep (1..4096 new tokens "
                          "per sequence per step, 64 sequences, INT4) as one JSON line")
@@ -831,6 +834,10 @@ def main():
         if args.layers < 1:
             raise SystemExit("--layers must be >= 1")
         w["layers"] = args.layers
+    if args.batch is not None:
+        if args.batch < 1:
+            raise SystemExit("--batch must be >= 1")
+        w["batch"] = args.batch
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -287,6 +287,24 @@ MG_API mg_status mg_paged_decode_attention_planned(const mg_cache_layout* layout
                                             float scale, void* out, int32_t out_dtype, void* workspace,
                                             int64_t workspace_bytes, int32_t* dev_status, mg_stream_t stream);
 
+/* mg_paged_decode_attention_planned with launch flags (the plain form passes 0).
+ * MG_ATTN_PLAN_SETTLED: the plan, the block tables and the allocation status
+ * (mg_plan_append) were written by launches that precede the launch right
+ * before this one on the stream, and that launch either is not a programmatic
+ * dependent launch or waits for its own prerequisites before it releases its
+ * dependents (every kernel of this library does; a plain launch does).  The
+ * kernel then reads the plan and warms L2 with its first pages before it waits
+ * for that launch to finish, on the SMs it has already left.  Never set it on
+ * the launch right after mg_paged_decode_plan.  An unknown flag is
+ * MG_ERR_INVALID_ARGUMENT. */
+#define MG_ATTN_PLAN_SETTLED 0x1u
+MG_API mg_status mg_paged_decode_attention_planned_flags(const mg_cache_layout* layout, const mg_layer_ptrs* layer,
+                                                  const int32_t* block_tables, const void* plan,
+                                                  int64_t plan_bytes, int32_t batch, const void* q,
+                                                  int32_t q_dtype, int32_t num_q_heads, float scale, void* out,
+                                                  int32_t out_dtype, void* workspace, int64_t workspace_bytes,
+                                                  uint32_t flags, int32_t* dev_status, mg_stream_t stream);
+
 /* Standalone block gather + dequantize (the batched read_fp32 of
  * metagross/cache.py:74-85): for each sequence b, its committed pages in
  * block-table order, then (include_staging != 0) the exact staged tail, are

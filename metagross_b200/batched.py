@@ -105,6 +105,7 @@ class BatchedPagedKVCache:
         self._ws_key = None
         self._plan = None
         self._plan_ok = False
+        self._plan_last = False  # the plan kernel is the cache's latest launch (nothing after it yet)
 
     # ------------------------------------------------------------------ steps
     def begin_step(self, n_new) -> None:
@@ -134,6 +135,7 @@ class BatchedPagedKVCache:
         _get_C().kv_append(self.k_pool[layer], self.v_pool[layer], self.k_scales[layer], self.v_scales[layer],
                            self.staging_k[layer], self.staging_v[layer], self.block_tables, self.seq_lens,
                            self.n_new, k_new, v_new, self.status)
+        self._plan_last = False
 
     def append_rope(self, layer: int, qkv: torch.Tensor, num_q_heads: int, cos: torch.Tensor, sin: torch.Tensor,
                     q_out: torch.Tensor) -> None:
@@ -148,10 +150,19 @@ class BatchedPagedKVCache:
         _get_C().kv_append_rope(self.k_pool[layer], self.v_pool[layer], self.k_scales[layer], self.v_scales[layer],
                                 self.staging_k[layer], self.staging_v[layer], self.block_tables, self.seq_lens,
                                 self.n_new, qkv, num_q_heads, cos, sin, q_out, self.status)
+        self._plan_last = False
 
     def invalidate_plan(self) -> None:
         """Mark the decode plan stale (after writing seq_lens or block_tables directly)."""
         self._plan_ok = False
+
+    def prepare_plan(self) -> None:
+        """Build the step's decode plan now if the lengths changed since the last
+        one (right after ``begin_step``, before the step's first append): the
+        attention launches that follow a launch other than the plan's then read
+        it, and warm L2 with their first pages, before they wait for that launch
+        (MG_ATTN_PLAN_SETTLED)."""
+        self._decode_plan()
 
     def _decode_plan(self) -> torch.Tensor:
         """The step's decode plan, rebuilt on the device when the lengths changed."""
@@ -161,6 +172,7 @@ class BatchedPagedKVCache:
         if not self._plan_ok:
             C.decode_plan(self.k_pool[0], self.block_tables, self.seq_lens, True, self._plan, self.status)
             self._plan_ok = True
+            self._plan_last = True
         return self._plan
 
     def _workspace(self, num_q_heads: int, max_context: int) -> torch.Tensor:
@@ -188,10 +200,13 @@ class BatchedPagedKVCache:
         if out is None:
             out = torch.empty_like(q)
         plan = self._decode_plan()
+        # settled: the plan kernel is not the launch right before this one (an
+        # append or another attention of the cache came in between)
         _get_C().paged_decode_attention_planned(q.contiguous(), self.k_pool[layer], self.v_pool[layer],
                                                 self.k_scales[layer], self.v_scales[layer], self.staging_k[layer],
                                                 self.staging_v[layer], self.block_tables, plan, sc, ws, out,
-                                                self.status)
+                                                self.status, settled=not self._plan_last)
+        self._plan_last = False
         return out
 
     def gather(self, layer: int, dtype=torch.float32, include_staging: bool = True):
@@ -258,7 +273,8 @@ class BatchedPagedKVCache:
 
 class DecodeGraph:
     """One decode step over every layer of ``cache`` captured as a CUDA graph:
-    begin_step(n_new) (page allocation), the step's decode plan, then per layer
+    begin_step(n_new) (page allocation), the step's decode plan (before the
+    first append, so that every attention launch reads it early), then per layer
     append(k_new[l], v_new[l]) and attend(q[l]) -> out[l], all on the fixed
     device buffers given here.  ``replay()`` runs a step with one launch from
     the host, so the step is bound by the GPU, not by per-kernel launch cost.
@@ -292,6 +308,7 @@ class DecodeGraph:
     def _step(self):
         c = self.cache
         c.begin_step(self.n_new)
+        c.prepare_plan()
         for layer in range(c.num_layers):
             c.append(layer, self.k_new[layer], self.v_new[layer])
             c.attend(layer, self.q[layer], scale=self.scale, out=self.out[layer],

@@ -508,7 +508,8 @@ void paged_decode_attention_planned(torch::Tensor q, torch::Tensor k_pool, torch
                                     torch::Tensor k_scales, torch::Tensor v_scales,
                                     c10::optional<torch::Tensor> staging_k, c10::optional<torch::Tensor> staging_v,
                                     torch::Tensor block_tables, torch::Tensor plan, double scale,
-                                    torch::Tensor workspace, torch::Tensor out, c10::optional<torch::Tensor> status) {
+                                    torch::Tensor workspace, torch::Tensor out, c10::optional<torch::Tensor> status,
+                                    bool settled) {
     const c10::cuda::CUDAGuard guard(q.device());
     auto p = make_pools(k_pool, v_pool, k_scales, v_scales, staging_k, staging_v, block_tables);
     const int64_t B = block_tables.size(0);
@@ -520,12 +521,13 @@ void paged_decode_attention_planned(torch::Tensor q, torch::Tensor k_pool, torch
     TORCH_CHECK(workspace.is_cuda() && workspace.is_contiguous(), "workspace must be a contiguous CUDA tensor");
     TORCH_CHECK(plan.is_cuda() && plan.is_contiguous() && plan.scalar_type() == torch::kUInt8,
                 "plan must be a contiguous CUDA uint8 tensor");
-    check_status(mg_paged_decode_attention_planned(
+    check_status(mg_paged_decode_attention_planned_flags(
                      &p.L, &p.ptrs, block_tables.data_ptr<int32_t>(), plan.data_ptr(), plan.numel(),
                      static_cast<int32_t>(B), q.data_ptr(), float_code(q, "q"), static_cast<int32_t>(q.size(1)),
                      static_cast<float>(scale), out.data_ptr(), float_code(out, "out"),
                      workspace.numel() > 0 ? workspace.data_ptr() : nullptr,
-                     workspace.numel() * workspace.element_size(), status_ptr(status), cur_stream()),
+                     workspace.numel() * workspace.element_size(), settled ? MG_ATTN_PLAN_SETTLED : 0u,
+                     status_ptr(status), cur_stream()),
                  "paged_decode_attention_planned");
 }
 
@@ -651,11 +653,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           pybind11::arg("k_pool"), pybind11::arg("block_tables"), pybind11::arg("seq_lens"),
           pybind11::arg("with_staging"), pybind11::arg("plan"), pybind11::arg("status") = pybind11::none());
     m.def("paged_decode_attention_planned", &paged_decode_attention_planned,
-          "Fused batched paged decode attention with a prebuilt decode plan", pybind11::arg("q"),
-          pybind11::arg("k_pool"), pybind11::arg("v_pool"), pybind11::arg("k_scales"), pybind11::arg("v_scales"),
-          pybind11::arg("staging_k"), pybind11::arg("staging_v"), pybind11::arg("block_tables"), pybind11::arg("plan"),
-          pybind11::arg("scale"), pybind11::arg("workspace"), pybind11::arg("out"),
-          pybind11::arg("status") = pybind11::none());
+          "Fused batched paged decode attention with a prebuilt decode plan (settled: MG_ATTN_PLAN_SETTLED)",
+          pybind11::arg("q"), pybind11::arg("k_pool"), pybind11::arg("v_pool"), pybind11::arg("k_scales"),
+          pybind11::arg("v_scales"), pybind11::arg("staging_k"), pybind11::arg("staging_v"),
+          pybind11::arg("block_tables"), pybind11::arg("plan"), pybind11::arg("scale"), pybind11::arg("workspace"),
+          pybind11::arg("out"), pybind11::arg("status") = pybind11::none(), pybind11::arg("settled") = false);
     m.def("gather_dequant", &gather_dequant, "Block-table gather + dequantize of whole sequences",
           pybind11::arg("k_pool"), pybind11::arg("v_pool"), pybind11::arg("k_scales"), pybind11::arg("v_scales"),
           pybind11::arg("staging_k"), pybind11::arg("staging_v"), pybind11::arg("block_tables"),

@@ -474,13 +474,15 @@ extern "C" mg_status mg_paged_decode_plan(const mg_cache_layout* L, const int32_
                               static_cast<int32_t*>(plan), plan_bytes, dev_status, as_stream(stream));
 }
 
-extern "C" mg_status mg_paged_decode_attention_planned(const mg_cache_layout* L, const mg_layer_ptrs* lp,
-                                                       const int32_t* block_tables, const void* plan,
-                                                       int64_t plan_bytes, int32_t batch, const void* q,
-                                                       int32_t q_dtype, int32_t num_q_heads, float scale, void* out,
-                                                       int32_t out_dtype, void* workspace, int64_t workspace_bytes,
-                                                       int32_t* dev_status, mg_stream_t stream) {
+extern "C" mg_status mg_paged_decode_attention_planned_flags(const mg_cache_layout* L, const mg_layer_ptrs* lp,
+                                                             const int32_t* block_tables, const void* plan,
+                                                             int64_t plan_bytes, int32_t batch, const void* q,
+                                                             int32_t q_dtype, int32_t num_q_heads, float scale,
+                                                             void* out, int32_t out_dtype, void* workspace,
+                                                             int64_t workspace_bytes, uint32_t flags,
+                                                             int32_t* dev_status, mg_stream_t stream) {
     MG_REQUIRE(batch >= 0, "batch must be >= 0");
+    MG_REQUIRE((flags & ~MG_ATTN_PLAN_SETTLED) == 0, "unknown attention flags 0x%x", flags);
     if (batch == 0) return MG_OK;
     DecodeParams p;
     DecodePlan pl;
@@ -490,7 +492,19 @@ extern "C" mg_status mg_paged_decode_attention_planned(const mg_cache_layout* L,
     if (st != MG_OK) return st;
     MG_REQUIRE(plan && aligned16(plan) && plan_bytes >= p.lay.words * 4, "decode plan missing, unaligned or too small");
     p.plan = static_cast<const int32_t*>(plan);
+    p.plan_settled = (flags & MG_ATTN_PLAN_SETTLED) ? 1 : 0;
     return launch_any(L->kv_dtype == MG_KV_INT4, L->head_dim, p, pl, tl, as_stream(stream));
+}
+
+extern "C" mg_status mg_paged_decode_attention_planned(const mg_cache_layout* L, const mg_layer_ptrs* lp,
+                                                       const int32_t* block_tables, const void* plan,
+                                                       int64_t plan_bytes, int32_t batch, const void* q,
+                                                       int32_t q_dtype, int32_t num_q_heads, float scale, void* out,
+                                                       int32_t out_dtype, void* workspace, int64_t workspace_bytes,
+                                                       int32_t* dev_status, mg_stream_t stream) {
+    return mg_paged_decode_attention_planned_flags(L, lp, block_tables, plan, plan_bytes, batch, q, q_dtype,
+                                                   num_q_heads, scale, out, out_dtype, workspace, workspace_bytes, 0u,
+                                                   dev_status, stream);
 }
 
 extern "C" mg_status mg_paged_decode_attention(const mg_cache_layout* L, const mg_layer_ptrs* lp,

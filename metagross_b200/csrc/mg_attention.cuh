@@ -93,6 +93,9 @@ constexpr int kTailUnits = 2;     // work units the plan charges for a staged ta
 constexpr int kPlanInline = 4;    // records per CTA in the inline area
 constexpr int kPlanPids = 128;    // page ids per CTA in the plan
 constexpr int kRecCache = 64;     // records an attention CTA keeps in shared memory
+// page bytes a CTA warms in L2 before its wait (settled plan): the first copies
+// only -- warming a whole 50 MB launch (384 KB a CTA) this way delayed them
+constexpr int kPrewarmBytes = 48 * 1024;
 struct PlanLayout {
     int off_counts, off_offs, off_recs, off_pids, off_flat, off_empty;
     int64_t words;
@@ -140,6 +143,11 @@ struct DecodeParams {
     float* ws_l;    // [2*G, Hq]
     uint32_t* tickets;  // [batch]
     int32_t* status;
+    // the plan, the block tables and the allocation status were written before
+    // the launch that immediately precedes this one (MG_ATTN_PLAN_SETTLED): the
+    // kernel reads them, and warms L2 with its first pages, before it waits for
+    // that launch to finish
+    int plan_settled;
     // bulk-copy kernel (mg_attention_tma.cuh): dynamic shared memory layout,
     // offsets from the 1024-byte aligned base
     int tma_ns;           // stages in the ring

@@ -664,8 +664,14 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
     __shared__ int sm_hdr[3];
     __shared__ int sm_last[2 * 2 * kWarps];  // (cut segment, head of the warp, kv-head group): this CTA merges
 
-    grid_dependency_wait();
-    grid_launch_dependents();
+    // With a settled plan the prologue (plan, status) and an L2 warm-up of the
+    // first pages run before the wait on the previous launch, on SMs that launch
+    // has already left; nothing is written to global memory before it.
+    const bool settled = p.plan_settled != 0;
+    if (!settled) {
+        grid_dependency_wait();
+        grid_launch_dependents();
+    }
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, c = lane & 3;
@@ -683,6 +689,7 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
     // round trip (all lie inside buffers the host sized); a step whose allocation
     // failed then runs no segment and writes nothing. ------------------------------
     const int4* prec = reinterpret_cast<const int4*>(p.plan + p.lay.off_recs) + static_cast<int64_t>(cta) * kPlanInline * 2;
+    bool bad_plan = false;  // flagged after the wait (no global write before it)
     if (tid < 2 * kPlanInline) recs[tid] = __ldcg(prec + tid);
     const int4* ppid = reinterpret_cast<const int4*>(p.plan + p.lay.off_pids) + static_cast<int64_t>(cta) * (kPlanPids / 4);
     if (tid >= 32 && tid < 32 + kPlanPids / 4) reinterpret_cast<int4*>(spids)[tid - 32] = __ldcg(ppid + tid - 32);
@@ -693,7 +700,7 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
         const int32_t cnt = __ldcg(p.plan + p.lay.off_counts + cta), off = __ldcg(p.plan + p.lay.off_offs + cta);
         const bool stop = (stat & (MG_DEV_OUT_OF_PAGES | MG_DEV_BLOCK_TABLE_FULL | MG_DEV_BAD_LENGTH)) != 0;
         const bool ok = h0 == kPlanMagic && h1 == p.batch && h2 == static_cast<int>(gridDim.x) && h8 == p.has_staging;
-        if (!ok && !stop) flag(p.status, MG_DEV_BAD_ARGUMENT);
+        bad_plan = !ok && !stop;
         sm_hdr[0] = (ok && !stop) ? cnt : 0;
         sm_hdr[1] = (ok && !stop) ? h4 : 0;
         sm_hdr[2] = (ok && !stop) ? off : 0;
@@ -709,6 +716,27 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecodePa
     }
     // record k: shared memory for the first kRecCache, the flat array beyond
     auto rec = [&](int k) -> const int4* { return k < kRecCache ? recs + 2 * k : flat + 2 * k; };
+
+    if (settled) {
+        // the first segment's pages (up to kPrewarmBytes of this CTA's) into L2,
+        // a lane per page, from the last warp; the tile loads after the wait read
+        // them there (L2 is coherent with the previous launch's writes)
+        const bool aligned = ((reinterpret_cast<uintptr_t>(p.k_pool) | reinterpret_cast<uintptr_t>(p.v_pool) |
+                               static_cast<uintptr_t>(p.page_bytes)) & 15u) == 0;
+        if (warp == NCW - 1 && nseg > 0 && aligned) {
+            const int n0 = min(min(rec(0)[0].z, kPlanPids), static_cast<int>(kPrewarmBytes / (2 * p.page_bytes)));
+            for (int j = lane; j < n0; j += 32) {
+                const int32_t pid = spids[j];
+                if (pid >= 0 && pid < p.num_pages) {
+                    prefetch_l2_bulk(p.k_pool + static_cast<int64_t>(pid) * p.page_bytes, p.page_bytes);
+                    prefetch_l2_bulk(p.v_pool + static_cast<int64_t>(pid) * p.page_bytes, p.page_bytes);
+                }
+            }
+        }
+        grid_dependency_wait();
+        grid_launch_dependents();
+    }
+    if (bad_plan) flag(p.status, MG_DEV_BAD_ARGUMENT);
 
     // empty sequences: zeros (normalised) or (0, 0, -inf) (unnormalised)
     for (int i = cta; i < n_empty; i += gridDim.x) {

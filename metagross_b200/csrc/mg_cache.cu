@@ -339,6 +339,11 @@ __global__ void __launch_bounds__(kAppendThreads, KEEP <= 2 ? 4 : 2) kv_append_k
     constexpr int kKeep = KEEP;
     __shared__ float red[32];
     const int b = blockIdx.x, jj = blockIdx.y, kv = blockIdx.z;
+    // launched as a programmatic dependent launch: the new tokens come from the
+    // previous launch; releasing the next one at once lets an attention launch
+    // read its plan while this one runs
+    grid_dependency_wait();
+    grid_launch_dependents();
     // status, length and count in one round trip
     const int32_t stat = p.status ? *(volatile int32_t*)p.status : 0;
     const int new_len = p.seq_lens[b], add = p.n_new[b];
@@ -733,14 +738,23 @@ mg_status append_launch(const mg_cache_layout* L, const mg_layer_ptrs* lp, const
     const bool s16 = L->staging_dtype == MG_F16, n16 = new_dtype == MG_F16;
     cudaStream_t s = as_stream(stream);
     const bool small = static_cast<int64_t>(L->page_size) * p.row <= static_cast<int64_t>(kAppendThreads) * 8 * 2;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kAppendThreads);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     auto go = [&](auto keep) {
         constexpr int K = decltype(keep)::value;
-        if (!i4 && s16 && n16) kv_append_kernel<false, __half, __half, K><<<grid, kAppendThreads, 0, s>>>(p);
-        else if (!i4 && !s16 && n16) kv_append_kernel<false, float, __half, K><<<grid, kAppendThreads, 0, s>>>(p);
-        else if (!i4 && !s16 && !n16) kv_append_kernel<false, float, float, K><<<grid, kAppendThreads, 0, s>>>(p);
-        else if (i4 && s16 && n16) kv_append_kernel<true, __half, __half, K><<<grid, kAppendThreads, 0, s>>>(p);
-        else if (i4 && !s16 && n16) kv_append_kernel<true, float, __half, K><<<grid, kAppendThreads, 0, s>>>(p);
-        else kv_append_kernel<true, float, float, K><<<grid, kAppendThreads, 0, s>>>(p);
+        if (!i4 && s16 && n16) cudaLaunchKernelEx(&cfg, kv_append_kernel<false, __half, __half, K>, p);
+        else if (!i4 && !s16 && n16) cudaLaunchKernelEx(&cfg, kv_append_kernel<false, float, __half, K>, p);
+        else if (!i4 && !s16 && !n16) cudaLaunchKernelEx(&cfg, kv_append_kernel<false, float, float, K>, p);
+        else if (i4 && s16 && n16) cudaLaunchKernelEx(&cfg, kv_append_kernel<true, __half, __half, K>, p);
+        else if (i4 && !s16 && n16) cudaLaunchKernelEx(&cfg, kv_append_kernel<true, float, __half, K>, p);
+        else cudaLaunchKernelEx(&cfg, kv_append_kernel<true, float, float, K>, p);
     };
     if (small) go(std::integral_constant<int, 2>{});
     else go(std::integral_constant<int, 8>{});

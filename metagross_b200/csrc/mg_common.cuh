@@ -257,6 +257,11 @@ __device__ __forceinline__ void cp_async_wait_group() {
 __device__ __forceinline__ void prefetch_l1(const void* ptr) { asm volatile("prefetch.global.L1 [%0];" ::"l"(ptr)); }
 // Non-blocking hint: bring the line holding ptr into L2 (coherent with every writer).
 __device__ __forceinline__ void prefetch_l2(const void* ptr) { asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr)); }
+// Non-blocking hint: bring [ptr, ptr + bytes) into L2; ptr 16-byte aligned,
+// bytes a multiple of 16.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* ptr, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ptr), "r"(bytes) : "memory");
+}
 // Barrier among the nthreads (a multiple of 32) threads that use barrier id.
 __device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

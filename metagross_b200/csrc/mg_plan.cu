@@ -8,11 +8,13 @@
 // kTailUnits units, about what it costs next to a page.  A piece of the
 // tail's weight that falls into another CTA's range is an empty piece (no
 // pages, no tail; it merges as a zero partial).  Two partitions:
-//   chunk     when the non-empty sequences fit on the SMs: each sequence gets
-//             k_b = ceil(U_b / S) near-equal chunks with S the smallest chunk
-//             size for which sum_b k_b <= #CTAs (so the longest chunk is as
-//             short as possible), and every CTA runs exactly one chunk of one
-//             sequence -- no CTA pays for a second sequence;
+//   chunk     when the non-empty sequences fit on the SMs and the split stays
+//             even: each sequence gets k_b = ceil(U_b / S) near-equal chunks
+//             with S the smallest chunk size for which sum_b k_b <= #CTAs (so
+//             the longest chunk is as short as possible), and every CTA runs
+//             exactly one chunk of one sequence -- no CTA pays for a second
+//             sequence.  Taken only while S <= max(5/4 of, or 16 units above,
+//             the even share W / min(W, #CTAs));
 //   stream-K  otherwise: CTA c takes units [c*W/G, (c+1)*W/G) of the
 //             flattened list, i.e. a few whole short sequences plus the cut
 //             ends of at most two others.
@@ -25,6 +27,13 @@ namespace mg {
 namespace {
 
 constexpr int kPlanThreads = 1024;
+// chunk mode while its longest chunk is within 5/4 of the even share, or within
+// kSegmentUnits units of it (measured on one B200: a 64-sequence batch of
+// 128..2048 tokens took 16.5 us per launch in chunks of at most 41 units and
+// 25.6 us in stream-K shares of 33; 128 log-normal contexts took 123 us in
+// chunks of at most 442 units and 74 us in stream-K shares of 193)
+constexpr int kChunkSlackNum = 5, kChunkSlackDen = 4;
+constexpr int kSegmentUnits = 16;
 
 struct PlanParams {
     const int32_t* block_tables;  // [batch, max_blocks]
@@ -133,8 +142,8 @@ __global__ void __launch_bounds__(kPlanThreads, 1) decode_plan_kernel(const Plan
     for (int b = threadIdx.x; b < B; b += blockDim.x)
         if (units[b] == 0) pp.plan[pp.lay.off_empty + aux2[b]] = b;
 
-    const bool chunk = W > 0 && nonempty <= G;
-    int used = 0;
+    bool chunk = W > 0 && nonempty <= G;
+    int S = 0;
     if (chunk) {
         // ---- smallest chunk size S with sum_b ceil(U_b / S) <= G -----------------
         int lo = (W + G - 1) / G, hi = maxu > lo ? maxu : lo;
@@ -146,7 +155,18 @@ __global__ void __launch_bounds__(kPlanThreads, 1) decode_plan_kernel(const Plan
             if (need <= G) hi = mid;
             else lo = mid + 1;
         }
-        const int S = lo;
+        S = lo;
+        // The longest chunk sets the launch's length: with few long sequences
+        // among many short ones (at most one chunk per CTA) it can be several
+        // times the even share W / min(W, G) that stream-K gives every CTA.  But
+        // a stream-K CTA pays for each further sequence it starts (its q, its
+        // page-id window, its partial and merge), about kSegmentUnits units.
+        const int64_t GR = min(W, G);
+        chunk = static_cast<int64_t>(S) * GR * kChunkSlackDen <= static_cast<int64_t>(W) * kChunkSlackNum ||
+                static_cast<int64_t>(S - kSegmentUnits) * GR <= static_cast<int64_t>(W);
+    }
+    int used = 0;
+    if (chunk) {
         for (int b = threadIdx.x; b < B; b += blockDim.x) tmp[b] = (units[b] + S - 1) / S;
         __syncthreads();
         used = block_scan_array(tmp, aux, B, scratch);  // aux[b]: first CTA of sequence b

@@ -174,6 +174,7 @@ class LlamaDecoder:
         c, C = self.cache, _get_C()
         x = self.w["embed"][self.ids]
         c.begin_step(1)
+        c.prepare_plan()
         for i in range(self.s.layers):
             qkv = self._norm(x, self.w[f"{i}.n1"]) @ self.w[f"{i}.wqkv"]
             if self.fused_rope:

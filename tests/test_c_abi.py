@@ -140,3 +140,16 @@ def test_append_rejects_more_pages_than_one_launch_covers():
            None, None)
     assert rc == 1
     assert b"65534 pages" in lib.mg_last_error()
+
+
+def test_planned_attention_rejects_unknown_flags_before_launch():
+    lib = ctypes.CDLL(LIB)
+    lib.mg_last_error.restype = ctypes.c_char_p
+    f = lib.mg_paged_decode_attention_planned_flags
+    f.restype = ctypes.c_int
+    L = _Layout(0, 1, 16, 4, 64, 64, 1024)
+    p = ctypes.c_void_p(1 << 20)  # never dereferenced: refused before launch
+    rc = f(ctypes.byref(L), p, p, p, ctypes.c_int64(1 << 20), 1, p, 1, 32, ctypes.c_float(0.125), p, 1, p,
+           ctypes.c_int64(1 << 20), ctypes.c_uint32(0x2), None, None)
+    assert rc == 1
+    assert b"unknown attention flags" in lib.mg_last_error()

@@ -52,7 +52,6 @@ def plan_ref(lens, P, max_blocks, has_staging, G):
     def tail_of(b):
         return lens[b] % P if has_staging else 0
 
-    used = 0
     if chunk:
         lo, hi = (W + G - 1) // G, max(max(units), (W + G - 1) // G)
         while lo < hi:
@@ -62,6 +61,10 @@ def plan_ref(lens, P, max_blocks, has_staging, G):
             else:
                 lo = mid + 1
         S = lo
+        # the longest chunk within 5/4 of, or 16 units above, the even share
+        chunk = S * min(W, G) * 4 <= W * 5 or (S - 16) * min(W, G) <= W
+    used = 0
+    if chunk:
         k = [(u + S - 1) // S for u in units]
         kpre = np.concatenate([[0], np.cumsum(k)])
         spl = [kk if kk > 1 else 0 for kk in k]
@@ -178,7 +181,7 @@ def _grid():
 
 
 @pytest.mark.parametrize("case", ["uniform32", "ragged64", "one_long", "tiny_many", "with_empty", "staging_off",
-                                  "more_than_sms", "all_empty"])
+                                  "more_than_sms", "all_empty", "skewed_fewer_than_sms"])
 def test_plan_matches_restatement(case):
     G = _grid()
     g = np.random.default_rng(sum(map(ord, case)))
@@ -198,12 +201,18 @@ def test_plan_matches_restatement(case):
         has_staging = False
     elif case == "more_than_sms":
         lens = g.lognormal(np.log(2048), 0.8, 1024).clip(1, 32768).astype(int).tolist()
+    elif case == "skewed_fewer_than_sms":
+        # fewer sequences than SMs, heavy-tailed: the longest chunk would be over twice the even share
+        lens = g.lognormal(np.log(2048), 1.0, 128).clip(1, 32768).astype(int).tolist()
+        lens[5] = 32768
     else:
         lens = [0, 0, 0]
     words, status, max_blocks, bt = build_plan(lens, has_staging=has_staging)
     assert status == 0
     ref = plan_ref(lens, 16, max_blocks, has_staging, G)
     check(words, ref, lens, 16, has_staging, G, bt)
+    if case == "skewed_fewer_than_sms":
+        assert ref["mode"] == 2  # stream-K although every sequence would fit on its own SMs
 
 
 def test_plan_flags_bad_lengths():
