@@ -192,6 +192,15 @@ MG_API mg_status mg_plan_append(const mg_allocator* alloc, int32_t* block_tables
                          int32_t* seq_lens, const int32_t* n_new, int32_t batch, int32_t page_size,
                          int32_t* dev_status, mg_stream_t stream);
 
+/* mg_plan_append (with layout's max_blocks and page_size) followed by
+ * mg_paged_decode_plan from the grown lengths, in one launch: a decode step's
+ * allocation and its attention plan.  Same results as the two calls in that
+ * order; batch in [1, 8192].  Issued before the step's first append, it
+ * leaves every attention launch of the step free to take MG_ATTN_PLAN_SETTLED. */
+MG_API mg_status mg_plan_step(const mg_allocator* alloc, const mg_cache_layout* layout, int32_t* block_tables,
+                       int32_t* seq_lens, const int32_t* n_new, int32_t batch, int32_t with_staging, void* plan,
+                       int64_t plan_bytes, int32_t* dev_status, mg_stream_t stream);
+
 /* Per layer, after mg_plan_append: write the step's new tokens.  k_new/v_new
  * [batch, max_new, Hkv, D] in new_dtype (f16 or f32); seq_lens are the lengths
  * AFTER the step, n_new the tokens added.  A page that fills is quantized with

@@ -98,6 +98,7 @@ class BatchedPagedKVCache:
         self.block_tables = torch.zeros(batch, self.max_blocks, dtype=torch.int32, device=self.device)
         self.seq_lens = torch.zeros(batch, dtype=torch.int32, device=self.device)
         self.n_new = torch.zeros(batch, dtype=torch.int32, device=self.device)
+        self._n_new_val = 0  # the one value every entry of n_new holds, or None
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.allocator = DeviceBlockAllocator(self.num_pages, self.device)
         self._max_len = 0  # host-side upper bound on seq_lens
@@ -108,13 +109,15 @@ class BatchedPagedKVCache:
         self._plan_last = False  # the plan kernel is the cache's latest launch (nothing after it yet)
 
     # ------------------------------------------------------------------ steps
-    def begin_step(self, n_new) -> None:
-        """Grow every sequence by n_new tokens (int or int32 tensor [B]); allocate the pages that fill."""
+    def begin_step(self, n_new, plan: bool = False) -> None:
+        """Grow every sequence by n_new tokens (int or int32 tensor [B]); allocate the pages that fill.
+        plan=True also builds the step's decode plan, in the same launch (mg_plan_step): call it so
+        before the step's first append, and every attention launch of the step reads its plan early."""
         C = _get_C()
         if isinstance(n_new, int):
             if n_new < 0:
                 raise ValueError("n_new must be >= 0")
-            self.n_new.fill_(n_new)
+            self._ensure_n_new(n_new)
             self._max_len += n_new
         else:
             t = torch.as_tensor(n_new, dtype=torch.int32)
@@ -123,10 +126,27 @@ class BatchedPagedKVCache:
             else:
                 self._max_len = self.max_blocks * self.page_size + self.page_size - 1
             self.n_new.copy_(t.to(self.device), non_blocking=True)
+            self._n_new_val = None
         self._max_len = min(self._max_len, self.max_blocks * self.page_size + self.page_size - 1)
+        if plan:
+            if self._plan is None:
+                self._plan = torch.zeros(C.decode_plan_bytes(self.batch), dtype=torch.uint8, device=self.device)
+            C.plan_step(self.allocator.free_stack, self.allocator.n_free, self.allocator.in_use, self.k_pool[0],
+                        self.block_tables, self.seq_lens, self.n_new, True, self._plan, self.status)
+            self._plan_ok = True
+            self._plan_last = True
+            return
         self._plan_ok = False
         C.plan_append(self.allocator.free_stack, self.allocator.n_free, self.allocator.in_use, self.block_tables,
                       self.seq_lens, self.n_new, self.page_size, self.status)
+        self._plan_last = False
+
+    def _ensure_n_new(self, n: int) -> None:
+        """Every entry of the device n_new equal to n; no launch when it already is (a
+        decode graph then replays without the fill)."""
+        if self._n_new_val != n:
+            self.n_new.fill_(n)
+            self._n_new_val = n
 
     def append(self, layer: int, k_new: torch.Tensor, v_new: torch.Tensor) -> None:
         """Write this step's tokens of one layer: k_new/v_new [B, T, Hkv, D] (fp16/fp32), n_new[b] <= T used."""
@@ -273,8 +293,9 @@ class BatchedPagedKVCache:
 
 class DecodeGraph:
     """One decode step over every layer of ``cache`` captured as a CUDA graph:
-    begin_step(n_new) (page allocation), the step's decode plan (before the
-    first append, so that every attention launch reads it early), then per layer
+    begin_step(n_new, plan=True) (page allocation and the step's decode plan in
+    one launch, before the first append, so that every attention launch reads
+    its plan early), then per layer
     append(k_new[l], v_new[l]) and attend(q[l]) -> out[l], all on the fixed
     device buffers given here.  ``replay()`` runs a step with one launch from
     the host, so the step is bound by the GPU, not by per-kernel launch cost.
@@ -293,9 +314,11 @@ class DecodeGraph:
                 raise ValueError(f"{name} must be a [{L}, ...] tensor on {cache.device}")
         self.cache, self.q, self.k_new, self.v_new, self.out = cache, q, k_new, v_new, out
         self.n_new, self.scale = n_new, scale
-        # buffers the step reuses must exist before capture
+        # buffers the step reuses must exist before capture; n_new is filled
+        # outside the graph (replay() refills it if an eager step changed it)
         cache._workspace(q.shape[2], cache.max_blocks * cache.page_size)
         cache._decode_plan()
+        cache._ensure_n_new(n_new)
         stream = torch.cuda.Stream(cache.device)
         stream.wait_stream(torch.cuda.current_stream(cache.device))
         self.graph = torch.cuda.CUDAGraph()
@@ -307,14 +330,14 @@ class DecodeGraph:
 
     def _step(self):
         c = self.cache
-        c.begin_step(self.n_new)
-        c.prepare_plan()
+        c.begin_step(self.n_new, plan=True)
         for layer in range(c.num_layers):
             c.append(layer, self.k_new[layer], self.v_new[layer])
             c.attend(layer, self.q[layer], scale=self.scale, out=self.out[layer],
                      max_context=c.max_blocks * c.page_size)
 
     def replay(self) -> None:
+        self.cache._ensure_n_new(self.n_new)
         self.graph.replay()
         self.cache._max_len = min(self.cache._max_len + self.n_new,
                                   self.cache.max_blocks * self.cache.page_size + self.cache.page_size - 1)

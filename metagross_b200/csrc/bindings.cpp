@@ -504,6 +504,34 @@ void decode_plan(torch::Tensor k_pool, torch::Tensor block_tables, torch::Tensor
                  "decode_plan");
 }
 
+void plan_step(torch::Tensor free_stack, torch::Tensor n_free, torch::Tensor in_use, torch::Tensor k_pool,
+               torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor n_new, bool with_staging,
+               torch::Tensor plan, c10::optional<torch::Tensor> status) {
+    const c10::cuda::CUDAGuard guard(free_stack.device());
+    auto a = make_alloc(free_stack, n_free, in_use);
+    TORCH_CHECK(k_pool.is_cuda() && k_pool.dim() == 4, "k_pool must be a 4-D CUDA tensor");
+    check_i32_vec(block_tables, 1, "block_tables");
+    TORCH_CHECK(block_tables.dim() == 2, "block_tables must be [batch, max_blocks]");
+    const int64_t B = block_tables.size(0);
+    check_i32_vec(seq_lens, B, "seq_lens");
+    check_i32_vec(n_new, B, "n_new");
+    TORCH_CHECK(plan.is_cuda() && plan.is_contiguous() && plan.scalar_type() == torch::kUInt8,
+                "plan must be a contiguous CUDA uint8 tensor");
+    mg_cache_layout L{};
+    const bool i4 = k_pool.scalar_type() == torch::kUInt8;
+    L.kv_dtype = i4 ? MG_KV_INT4 : MG_KV_INT8;
+    L.staging_dtype = MG_F16;
+    L.page_size = static_cast<int32_t>(k_pool.size(1));
+    L.num_kv_heads = static_cast<int32_t>(k_pool.size(2));
+    L.head_dim = static_cast<int32_t>(i4 ? k_pool.size(3) * 2 : k_pool.size(3));
+    L.max_blocks = static_cast<int32_t>(block_tables.size(1));
+    L.num_pages = k_pool.size(0);
+    check_status(mg_plan_step(&a, &L, block_tables.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(),
+                              n_new.data_ptr<int32_t>(), static_cast<int32_t>(B), with_staging ? 1 : 0,
+                              plan.data_ptr(), plan.numel(), status_ptr(status), cur_stream()),
+                 "plan_step");
+}
+
 void paged_decode_attention_planned(torch::Tensor q, torch::Tensor k_pool, torch::Tensor v_pool,
                                     torch::Tensor k_scales, torch::Tensor v_scales,
                                     c10::optional<torch::Tensor> staging_k, c10::optional<torch::Tensor> staging_v,
@@ -651,6 +679,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("decode_plan_bytes", &decode_plan_bytes, "Bytes of a decode plan for a batch");
     m.def("decode_plan", &decode_plan, "Build the step's decode plan (work split over the SMs) from seq_lens",
           pybind11::arg("k_pool"), pybind11::arg("block_tables"), pybind11::arg("seq_lens"),
+          pybind11::arg("with_staging"), pybind11::arg("plan"), pybind11::arg("status") = pybind11::none());
+    m.def("plan_step", &plan_step,
+          "plan_append then decode_plan in one launch: the step's allocation and its attention plan",
+          pybind11::arg("free_stack"), pybind11::arg("n_free"), pybind11::arg("in_use"), pybind11::arg("k_pool"),
+          pybind11::arg("block_tables"), pybind11::arg("seq_lens"), pybind11::arg("n_new"),
           pybind11::arg("with_staging"), pybind11::arg("plan"), pybind11::arg("status") = pybind11::none());
     m.def("paged_decode_attention_planned", &paged_decode_attention_planned,
           "Fused batched paged decode attention with a prebuilt decode plan (settled: MG_ATTN_PLAN_SETTLED)",

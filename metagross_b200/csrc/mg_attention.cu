@@ -17,7 +17,6 @@ namespace {
 int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 
 constexpr int64_t kSmemBudget = 220 * 1024;  // prefix + merge scratch + tail slots, one CTA per SM
-constexpr int kMaxBatch = 8192;              // the plan kernel keeps six ints per sequence in shared memory
 
 }  // namespace
 
@@ -300,8 +299,6 @@ mg_status launch(int kv4, int hd, const DecodeParams& p, const DecodePlan& pl, c
 bool aligned16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; }
 
 }  // namespace
-
-mg_status check_cache_layout(const mg_cache_layout* L);
 
 }  // namespace mg
 

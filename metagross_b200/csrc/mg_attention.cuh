@@ -101,9 +101,14 @@ struct PlanLayout {
     int64_t words;
 };
 PlanLayout plan_layout(int batch, int grid);
+constexpr int kMaxBatch = 8192;  // the plan kernel keeps six ints per sequence in shared memory
+mg_status check_cache_layout(const mg_cache_layout* L);  // mg_cache.cu
+
+struct AllocStep;
+// the step's decode plan; with alloc, the step's allocation first, in the same launch
 mg_status launch_decode_plan(const int32_t* block_tables, const int32_t* seq_lens, int32_t uniform_len, int batch,
                              int P, int max_blocks, int has_staging, int32_t* plan, int64_t plan_bytes,
-                             int32_t* status, cudaStream_t s);
+                             int32_t* status, cudaStream_t s, const AllocStep* alloc = nullptr);
 
 struct DecodeParams {
     const void* q;

@@ -9,6 +9,7 @@
 // allocators of one sequence all hand out the same ids).
 #include <type_traits>
 
+#include "mg_alloc_step.cuh"
 #include "mg_common.cuh"
 
 namespace mg {
@@ -26,71 +27,8 @@ __global__ void alloc_init_kernel(int32_t* free_stack, int32_t* n_free, int32_t*
     if (blockIdx.x == 0 && threadIdx.x == 0) *n_free = static_cast<int32_t>(n);
 }
 
-constexpr int32_t kStopBits = MG_DEV_OUT_OF_PAGES | MG_DEV_BLOCK_TABLE_FULL | MG_DEV_BAD_LENGTH;
-
-// One CTA.  Pass 1 validates the whole step, pass 2 applies it, so a failed
-// step changes nothing.
-__global__ void __launch_bounds__(kPlanThreads) plan_append_kernel(int32_t* free_stack, int32_t* n_free_p,
-                                                                   int32_t* in_use, int32_t* block_tables,
-                                                                   int32_t max_blocks, int32_t* seq_lens,
-                                                                   const int32_t* n_new, int32_t batch,
-                                                                   int32_t P, int32_t* status) {
-    __shared__ int scratch[33];
-    __shared__ int s_flags;
-    if (threadIdx.x == 0) s_flags = 0;
-    __syncthreads();
-    if (status && (*(volatile int32_t*)status & kStopBits)) {
-        if (threadIdx.x == 0) flag(status, MG_DEV_SKIPPED);
-        return;
-    }
-    int local = 0;
-    int bad = 0;  // bit 0: a row would overflow; bit 1: a negative length or count
-    for (int b = threadIdx.x; b < batch; b += blockDim.x) {
-        const int old = seq_lens[b], add = n_new[b];
-        if (add < 0 || old < 0) { bad |= 2; continue; }
-        const int nw = old + add;
-        if (nw / P > max_blocks) bad |= 1;
-        local += nw / P - old / P;
-    }
-    int total;
-    if (bad) atomicOr(&s_flags, bad);
-    (void)block_exclusive_scan(local, scratch, &total);
-    __syncthreads();
-    const int n_free = *n_free_p;
-    if (s_flags) {
-        if (threadIdx.x == 0)
-            flag(status, ((s_flags & 1) ? MG_DEV_BLOCK_TABLE_FULL : 0) | ((s_flags & 2) ? MG_DEV_BAD_LENGTH : 0));
-        return;
-    }
-    if (total > n_free) {
-        if (threadIdx.x == 0) flag(status, MG_DEV_OUT_OF_PAGES);
-        return;
-    }
-    int base = 0;
-    for (int start = 0; start < batch; start += blockDim.x) {
-        const int b = start + threadIdx.x;
-        int old = 0, nw = 0, c = 0;
-        if (b < batch) {
-            old = seq_lens[b];
-            nw = old + n_new[b];
-            c = nw / P - old / P;
-        }
-        int chunk_total;
-        const int excl = block_exclusive_scan(c, scratch, &chunk_total) + base;
-        if (b < batch) {
-            int32_t* row = block_tables + static_cast<int64_t>(b) * max_blocks;
-            for (int j = 0; j < c; ++j) {
-                const int32_t page = free_stack[n_free - 1 - (excl + j)];
-                row[old / P + j] = page;
-                in_use[page] = 1;
-            }
-            seq_lens[b] = nw;
-        }
-        base += chunk_total;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) *n_free_p = n_free - total;
-}
+// One CTA: the step's allocation (mg_alloc_step.cuh).
+__global__ void __launch_bounds__(kPlanThreads) plan_append_kernel(AllocStep a) { alloc_step(a); }
 
 // Frees the listed sequences' pages beyond new_lens (0 when new_lens is
 // null) in (list order, block-table order): the order in which the
@@ -641,9 +579,9 @@ extern "C" mg_status mg_plan_append(const mg_allocator* a, int32_t* block_tables
     if (batch == 0) return MG_OK;
     MG_REQUIRE(block_tables && seq_lens && n_new, "null pointer");
     MG_REQUIRE(page_size >= 1 && max_blocks >= 1, "page_size and max_blocks must be positive");
-    plan_append_kernel<<<1, kPlanThreads, 0, as_stream(stream)>>>(a->free_stack, a->n_free, a->in_use, block_tables,
-                                                                  max_blocks, seq_lens, n_new, batch, page_size,
-                                                                  dev_status);
+    const AllocStep st{a->free_stack, a->n_free, a->in_use, block_tables, max_blocks, seq_lens, n_new, batch,
+                       page_size, dev_status};
+    plan_append_kernel<<<1, kPlanThreads, 0, as_stream(stream)>>>(st);
     return check_launch("plan_append_kernel");
 }
 

@@ -20,6 +20,7 @@
 //             ends of at most two others.
 // A sequence cut into several pieces gets one partial (m, l, acc) slot per
 // piece, contiguous from pbase; the last piece to finish merges them.
+#include "mg_alloc_step.cuh"
 #include "mg_attention.cuh"
 
 namespace mg {
@@ -96,11 +97,9 @@ __device__ __forceinline__ void write_rec(const PlanParams& pp, int cta, int off
     }
 }
 
-__global__ void __launch_bounds__(kPlanThreads, 1) decode_plan_kernel(const PlanParams pp) {
+__device__ __forceinline__ void decode_plan_body(const PlanParams& pp) {
     extern __shared__ __align__(16) int psm[];
     __shared__ int scratch[33];
-    grid_dependency_wait();
-    grid_launch_dependents();
     const int B = pp.batch, P = pp.P, G = pp.grid;
     int* len = psm;             // [B]
     int* units = len + B;       // [B]
@@ -302,6 +301,23 @@ __global__ void __launch_bounds__(kPlanThreads, 1) decode_plan_kernel(const Plan
     }
 }
 
+__global__ void __launch_bounds__(kPlanThreads, 1) decode_plan_kernel(const PlanParams pp) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    decode_plan_body(pp);
+}
+
+// A decode step's allocation, then its plan from the grown lengths, in one CTA
+// (mg_plan_step): the plan reads the lengths and block-table rows the
+// allocation wrote, after a CTA barrier.
+__global__ void __launch_bounds__(kPlanThreads, 1) step_plan_kernel(const AllocStep a, const PlanParams pp) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    alloc_step(a);
+    __syncthreads();
+    decode_plan_body(pp);
+}
+
 }  // namespace
 
 PlanLayout plan_layout(int batch, int grid) {
@@ -318,7 +334,7 @@ PlanLayout plan_layout(int batch, int grid) {
 
 mg_status launch_decode_plan(const int32_t* block_tables, const int32_t* seq_lens, int32_t uniform_len, int batch,
                              int P, int max_blocks, int has_staging, int32_t* plan, int64_t plan_bytes,
-                             int32_t* status, cudaStream_t s) {
+                             int32_t* status, cudaStream_t s, const AllocStep* alloc) {
     const int G = sm_count();
     const PlanLayout lay = plan_layout(batch, G);
     MG_REQUIRE(plan && plan_bytes >= static_cast<int64_t>(lay.words) * 4, "decode plan buffer too small: %lld < %lld",
@@ -338,14 +354,19 @@ mg_status launch_decode_plan(const int32_t* block_tables, const int32_t* seq_len
     pp.status = status;
     const size_t tmp_ints = static_cast<size_t>(batch > 2 * G + 1 ? batch : 2 * G + 1);
     const size_t smem = (static_cast<size_t>(5) * batch + 3 + tmp_ints + 3 * static_cast<size_t>(G)) * sizeof(int);
-    static int64_t attr_set[64] = {0};
+    // the dynamic shared-memory opt-in, per kernel and device (raised as batches grow)
+    static int64_t attr_set[2][64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (smem > 48 * 1024 && (dev < 0 || dev >= 64 || attr_set[dev] < static_cast<int64_t>(smem))) {
+    const int ki = alloc ? 1 : 0;
+    if (smem > 48 * 1024 && (dev < 0 || dev >= 64 || attr_set[ki][dev] < static_cast<int64_t>(smem))) {
         const cudaError_t e =
-            cudaFuncSetAttribute(decode_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+            alloc ? cudaFuncSetAttribute(step_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem))
+                  : cudaFuncSetAttribute(decode_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
         if (e != cudaSuccess) return set_error(MG_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-        if (dev >= 0 && dev < 64) attr_set[dev] = static_cast<int64_t>(smem);
+        if (dev >= 0 && dev < 64) attr_set[ki][dev] = static_cast<int64_t>(smem);
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(1);
@@ -357,9 +378,30 @@ mg_status launch_decode_plan(const int32_t* block_tables, const int32_t* seq_len
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    if (alloc) {
+        const cudaError_t e = cudaLaunchKernelEx(&cfg, step_plan_kernel, *alloc, pp);
+        if (e != cudaSuccess) return set_error(MG_ERR_CUDA, "step_plan_kernel launch: %s", cudaGetErrorString(e));
+        return check_launch("step_plan_kernel");
+    }
     const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_plan_kernel, pp);
     if (e != cudaSuccess) return set_error(MG_ERR_CUDA, "decode_plan_kernel launch: %s", cudaGetErrorString(e));
     return check_launch("decode_plan_kernel");
 }
 
 }  // namespace mg
+
+using namespace mg;
+
+extern "C" mg_status mg_plan_step(const mg_allocator* a, const mg_cache_layout* L, int32_t* block_tables,
+                                  int32_t* seq_lens, const int32_t* n_new, int32_t batch, int32_t with_staging,
+                                  void* plan, int64_t plan_bytes, int32_t* dev_status, mg_stream_t stream) {
+    MG_REQUIRE(a && a->free_stack && a->n_free && a->in_use, "null allocator pointer");
+    mg_status st = check_cache_layout(L);
+    if (st != MG_OK) return st;
+    MG_REQUIRE(batch >= 1 && batch <= kMaxBatch, "batch must be in [1, %d], got %d", kMaxBatch, batch);
+    MG_REQUIRE(block_tables && seq_lens && n_new, "null pointer");
+    const AllocStep as{a->free_stack, a->n_free, a->in_use, block_tables, L->max_blocks, seq_lens, n_new, batch,
+                       L->page_size, dev_status};
+    return launch_decode_plan(block_tables, seq_lens, -1, batch, L->page_size, L->max_blocks, with_staging ? 1 : 0,
+                              static_cast<int32_t*>(plan), plan_bytes, dev_status, as_stream(stream), &as);
+}

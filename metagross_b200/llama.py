@@ -173,8 +173,7 @@ class LlamaDecoder:
         o-projection GEMM accumulated into x, then the MLP."""
         c, C = self.cache, _get_C()
         x = self.w["embed"][self.ids]
-        c.begin_step(1)
-        c.prepare_plan()
+        c.begin_step(1, plan=True)
         for i in range(self.s.layers):
             qkv = self._norm(x, self.w[f"{i}.n1"]) @ self.w[f"{i}.wqkv"]
             if self.fused_rope:
@@ -196,6 +195,7 @@ class LlamaDecoder:
         c = self.cache
         c._workspace(self.s.heads, c.max_blocks * c.page_size)
         c._decode_plan()
+        c._ensure_n_new(1)  # filled outside the graph
         st = torch.cuda.Stream(self.device)
         st.wait_stream(torch.cuda.current_stream(self.device))
         self.graph = torch.cuda.CUDAGraph()
@@ -218,6 +218,7 @@ class LlamaDecoder:
             if t + 1 == n:
                 break
             if self.graph is not None:
+                c._ensure_n_new(1)
                 self.graph.replay()
                 c._max_len = min(c._max_len + 1, c.max_blocks * c.page_size + c.page_size - 1)
                 c._plan_ok = False

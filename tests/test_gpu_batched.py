@@ -352,3 +352,36 @@ def test_append_rounds_half_integer_quotients_like_the_reference(kv):
     cache.check()
     _assert_state_equal(cache, model)
     assert all(model.k_scales[int(model.block_tables[b, 0])] == 1.0 for b in range(B))
+
+
+@pytest.mark.parametrize("case", ["grow", "out_of_pages", "prefill"])
+def test_plan_step_equals_plan_append_then_plan(case):
+    """mg_plan_step (allocation + decode plan in one launch) leaves the same
+    lengths, block tables, free stack, status and plan bytes as mg_plan_append
+    followed by mg_paged_decode_plan."""
+    B, H, D, P = 40, 4, 64, 16
+    g = np.random.default_rng(3)
+    caches = [_cache_cls()(1, B, H, D, page_size=P, num_pages=B * 70 if case != "out_of_pages" else 300,
+                           max_blocks=70, kv_dtype="int4") for _ in range(2)]
+    lens = torch.tensor(g.integers(0, 600, B), dtype=torch.int32)
+    if case == "out_of_pages":
+        lens = torch.tensor(g.integers(0, 120, B), dtype=torch.int32)
+    for c in caches:
+        c.begin_step(lens)
+    steps = [torch.tensor(g.integers(0, 40, B), dtype=torch.int32)] if case != "grow" else [1] * 20
+    if case == "out_of_pages":
+        steps = [torch.full((B,), 200, dtype=torch.int32)]
+    for n in steps:
+        a, b = caches
+        a.begin_step(n)
+        a._decode_plan()
+        b.begin_step(n, plan=True)
+        torch.cuda.synchronize()
+        assert torch.equal(a.seq_lens, b.seq_lens)
+        assert torch.equal(a.block_tables, b.block_tables)
+        assert torch.equal(a.status, b.status)
+        assert a.allocator.free_list() == b.allocator.free_list()
+        assert torch.equal(a._plan, b._plan)
+    if case == "out_of_pages":
+        assert int(caches[1].status.item()) & 0x1  # MG_DEV_OUT_OF_PAGES, nothing grew
+        assert torch.equal(caches[1].seq_lens, lens.cuda())
