@@ -901,10 +901,14 @@ def main():
         achieved = m["att_bytes_per_launch"] / (m["att_avg_ms"] / 1e3) / 1e9
         seq_steps = m["tot_batch"] * args.steps / (m["ms"] / 1e3)
         # which attention kernel ran: every workload here has 16-token pages, page scales, fp16 staging and
-        # head_dim 64, so the pool's code width decides (the rule of tma_applies in csrc/mg_attention.cu)
+        # head_dim 64, so the pool's code width decides (the rule of tma_mode in csrc/mg_attention.cu)
         force = os.environ.get("METAGROSS_B200_ATTENTION", "")
-        bulk = force == "bulk" or (force != "registers" and w["kv"] == "int8")
-        kernel = "paged_decode_tma_kernel" if bulk else "paged_decode_kernel"
+        if force == "registers":
+            kernel = "paged_decode_kernel"
+        elif w["kv"] == "int8" or force == "bulk":
+            kernel = "paged_decode_tma_kernel"
+        else:
+            kernel = "paged_decode_tma_kernel (self-copying mode)"
         line = {
             "metric": metric, "value": round(m["value"], 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": m["ms"] / args.steps, "higher_is_better": True,

@@ -103,39 +103,72 @@ namespace {
 // ---------------------------------------------------------------------------
 constexpr int64_t kTmaSmemLimit = 232448 - 1024;  // 227 KB per CTA, less the static arrays and slack
 
-// The layout the bulk-copy kernel serves (mg_attention_tma.cuh): INT8 pages.
-// INT4 pages of the TinyLlama attention shape are 2 KB per K or V copy, and
-// streams of 2 KB copies measured 0.9-1.7 TB/s (a per-SM rate of copies, not
-// of bytes) against 5-6 TB/s for 12 KB pages, so the register-streaming kernel
-// serves INT4 (it measured 395 against 520-606 us on the 1024-sequence
-// log-normal INT4 launch).  The environment variable
-// METAGROSS_B200_ATTENTION=registers selects the register kernel for every
-// call, =bulk the bulk-copy kernel for INT4 pools too.
-bool tma_applies(const mg_cache_layout* L, bool staged) {
+// The layout the bulk-copy kernel serves (mg_attention_tma.cuh).  INT8 pages
+// stream through its producer's bulk copies.  INT4 pages of the TinyLlama
+// attention shape are 2 KB per K or V copy, and streams of 2 KB copies
+// measured 0.9-1.7 TB/s (a per-SM rate of copies, not of bytes) against 5-6
+// TB/s for 12 KB pages, so INT4 pools run the kernel's self-copying mode, whose
+// consumer warps cp.async their own tiles: on the 1024-sequence log-normal INT4
+// launch 371 us against 395 us on the register-streaming kernel and 520-606 us
+// with bulk copies (16.8 against 16.3 us on the short TinyLlama-shape launch).
+// The environment variable METAGROSS_B200_ATTENTION=registers selects the
+// register kernel for every call, =bulk the bulk copies for INT4 pools too.
+// 0: the register kernel; 1: the bulk-copy kernel; 2: its self-copying mode
+// (INT4 pools).
+int tma_mode(const mg_cache_layout* L, bool staged) {
     const char* sel = std::getenv("METAGROSS_B200_ATTENTION");
-    if (sel && std::strcmp(sel, "registers") == 0) return false;
-    if (L->kv_dtype == MG_KV_INT4 && !(sel && std::strcmp(sel, "bulk") == 0)) return false;
-    return L->page_size == 16 && L->scale_layout == MG_SCALE_PAGE && (!staged || L->staging_dtype == MG_F16) &&
-           (L->head_dim == 64 || L->head_dim == 128) && L->num_kv_heads >= 1 && L->num_kv_heads <= 15;
+    if (sel && std::strcmp(sel, "registers") == 0) return 0;
+    const bool layout_ok = L->page_size == 16 && L->scale_layout == MG_SCALE_PAGE &&
+                           (!staged || L->staging_dtype == MG_F16) && (L->head_dim == 64 || L->head_dim == 128) &&
+                           L->num_kv_heads >= 1 && L->num_kv_heads <= 15;
+    if (!layout_ok) return 0;
+    if (L->kv_dtype == MG_KV_INT8) return 1;
+    if (sel && std::strcmp(sel, "bulk") == 0) return 1;
+    return 2;
 }
 
 // Shape of the bulk-copy kernel for a plan `base` of the register kernel (same
 // work split, workspace and query-column layout).  False when the pages do not
 // fit two stages.
-bool make_tma_plan(const DecodePlan& base, int kv4, int hd, int Hkv, DecodePlan* out, DecodeParams* p) {
+bool make_tma_plan(const DecodePlan& base, int kv4, int hd, int Hkv, bool self_copy, DecodePlan* out,
+                   DecodeParams* p) {
     if (hd == 128 && base.nt > 1) return false;  // two n-tiles of head_dim 128 exceed 128 registers
     DecodePlan pl = base;
     const int wph = Hkv > 12 ? 1 : 12 / Hkv;  // consumer warps: 12, or one per kv head for 13-15
     pl.hpw = 1;
     pl.wph = wph;
     pl.nconsumers = Hkv * wph;
-    pl.nwarps = pl.nconsumers + 1;
+    pl.nwarps = pl.nconsumers + (self_copy ? 0 : 1);
     const int64_t rowb = kv4 ? hd / 2 : hd;
     const int64_t page = 16 * Hkv * rowb;
     const int64_t half = align_up(page, 1024);
     const int ncols = pl.split_mode ? 1 : 2;
     const int64_t prefix = align_up(static_cast<int64_t>(kRecCache) * 32 + kPlanPids * 4, 128);
     const int64_t scratch = wph > 1 ? align_up(static_cast<int64_t>(pl.nconsumers) * pl.nt * ncols * 4 * (hd + 2) * 4, 128) : 0;
+    if (self_copy) {
+        // per consumer warp: RS slots of one head's K and V tiles, then RS (K, V) scale pairs
+        const int rs = (kv4 ? hd : 2 * hd) * 16 <= 1024 ? 8 : 4;  // kSelfSlots
+        const int64_t slot = 2 * 16 * rowb;
+        const int64_t stage_off = align_up(prefix + scratch, 1024);
+        const int64_t meta_off = stage_off + static_cast<int64_t>(pl.nconsumers) * rs * slot;
+        const int64_t total = 1024 + meta_off + static_cast<int64_t>(pl.nconsumers) * rs * 8;
+        if (total > kTmaSmemLimit) return false;
+        pl.scratch_off = static_cast<int>(prefix);
+        pl.tail_off = 0;
+        pl.tail_slot = 0;
+        pl.smem_bytes = total;
+        p->nconsumers = pl.nconsumers;
+        p->wph = pl.wph;
+        p->scratch_off = pl.scratch_off;
+        p->tma_ns = rs;
+        p->tma_nsdiv = FastDiv(static_cast<uint32_t>(rs));
+        p->tma_stage_bytes = static_cast<int>(slot);
+        p->tma_stage_off = static_cast<int>(stage_off);
+        p->tma_bar_off = static_cast<int>(meta_off);
+        p->tma_meta_off = static_cast<int>(meta_off);
+        *out = pl;
+        return true;
+    }
     // the deepest ring (up to 64 stages) that fits; a consumer warp holds two of
     // its pages (WPH apart) at once, so the ring must be deeper than that span
     int ns = 64;
@@ -250,6 +283,7 @@ mg_status page_tensor_map(const void* pool, int64_t n, int hkv, int rowb, CUtens
 // A batched call's kernel: the bulk-copy one when `use`.
 struct TmaLaunch {
     bool use = false;
+    bool self_copy = false;  // the consumer warps copy their own tiles (no tensor maps)
     DecodePlan pl;
     CUtensorMap tk, tv;
 };
@@ -430,7 +464,16 @@ mg_status prepare_batched(const mg_cache_layout* L, const mg_layer_ptrs* lp, con
     p.status = dev_status;
     set_workspace(p, pl, num_q_heads, L->head_dim, workspace);
     tl->use = false;
-    if (tma_applies(L, staged) && make_tma_plan(pl, L->kv_dtype == MG_KV_INT4, L->head_dim, L->num_kv_heads, &tl->pl, &p)) {
+    tl->self_copy = false;
+    const int mode = tma_mode(L, staged);
+    if (mode == 2 &&
+        make_tma_plan(pl, L->kv_dtype == MG_KV_INT4, L->head_dim, L->num_kv_heads, true, &tl->pl, &p)) {
+        std::memset(&tl->tk, 0, sizeof(tl->tk));
+        std::memset(&tl->tv, 0, sizeof(tl->tv));
+        tl->use = true;
+        tl->self_copy = true;
+    } else if (mode == 1 &&
+               make_tma_plan(pl, L->kv_dtype == MG_KV_INT4, L->head_dim, L->num_kv_heads, false, &tl->pl, &p)) {
         const int rowb = L->kv_dtype == MG_KV_INT4 ? L->head_dim / 2 : L->head_dim;
         int ph_k = 0, ph_v = 0;
         st = page_tensor_map(lp->k_pool, L->num_pages, L->num_kv_heads, rowb, &tl->tk, &ph_k);
@@ -449,8 +492,12 @@ mg_status prepare_batched(const mg_cache_layout* L, const mg_layer_ptrs* lp, con
 mg_status launch_any(int kv4, int hd, const DecodeParams& p, const DecodePlan& pl, const TmaLaunch& tl,
                      cudaStream_t s) {
     if (!tl.use) return launch(kv4, hd, p, pl, s);
-    if (kv4) return hd == 64 ? launch_tma<true, 64>(p, tl.pl, tl.tk, tl.tv, s) : launch_tma<true, 128>(p, tl.pl, tl.tk, tl.tv, s);
-    return hd == 64 ? launch_tma<false, 64>(p, tl.pl, tl.tk, tl.tv, s) : launch_tma<false, 128>(p, tl.pl, tl.tk, tl.tv, s);
+    const bool sc = tl.self_copy;
+    if (kv4)
+        return hd == 64 ? launch_tma<true, 64>(p, tl.pl, tl.tk, tl.tv, s, sc)
+                        : launch_tma<true, 128>(p, tl.pl, tl.tk, tl.tv, s, sc);
+    return hd == 64 ? launch_tma<false, 64>(p, tl.pl, tl.tk, tl.tv, s, sc)
+                    : launch_tma<false, 128>(p, tl.pl, tl.tk, tl.tv, s, sc);
 }
 
 }  // namespace

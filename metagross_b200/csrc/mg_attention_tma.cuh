@@ -63,6 +63,12 @@
 namespace mg {
 
 template <bool KV4, int HD>
+struct TCfg;
+// slots of a consumer warp's private ring in the self-copying mode (a power of two)
+template <bool KV4, int HD>
+constexpr int kSelfSlots = (KV4 ? HD : 2 * HD) * 16 <= 1024 ? 8 : 4;
+
+template <bool KV4, int HD>
 struct TCfg {
     static constexpr int ROWB = KV4 ? HD / 2 : HD;   // bytes of one (token, kv head) row
     static constexpr int TILE = 16 * ROWB;            // one head's 16-token tile in a stage
@@ -469,7 +475,8 @@ __device__ __forceinline__ void tma_page_tiles(TmaHead<NT, HD / 16>& S, const ui
     __syncwarp();
     if (lane == 0) {
 #pragma unroll
-        for (int t = 0; t < NTL; ++t) mbar_arrive(empty[t]);
+        for (int t = 0; t < NTL; ++t)
+            if (empty[t]) mbar_arrive(empty[t]);  // (no barrier: the warp copied the tile itself)
     }
     float ks[NTL][2], vs[NTL][2];
     bool live[NTL][2];
@@ -597,6 +604,6 @@ mg_status tma_decode_plan(int kv4, int hd, int P, int Hkv, int Hq, int q_f16, in
                           int scale_th, int num_sm, DecodePlan* out);
 template <bool KV4, int HD>
 mg_status launch_tma(const DecodeParams& p, const DecodePlan& pl, const CUtensorMap& tk, const CUtensorMap& tv,
-                     cudaStream_t s);
+                     cudaStream_t s, bool self_copy);
 
 }  // namespace mg

@@ -7,8 +7,13 @@
 
 namespace mg {
 
-template <bool KV4, int HD, int NT, bool SPLIT, int NW>
-__global__ void __launch_bounds__((NW + 1) * 32, 1)
+// SELF: no producer warp; each consumer warp copies its own kv head's rows of
+// its pages (cp.async, 16 bytes a lane) into a private ring of p.tma_ns slots
+// laid out as the bulk copies lay out a head's tile, and waits on its own copy
+// groups -- for pools whose pages are too small for one bulk copy each to keep
+// up (a 16-token INT4 page of 4 kv heads is 2 KB).
+template <bool KV4, int HD, int NT, bool SPLIT, int NW, bool SELF>
+__global__ void __launch_bounds__((NW + (SELF ? 0 : 1)) * 32, 1)
     paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                             const DecodeParams p) {
     using T = TCfg<KV4, HD>;
@@ -26,8 +31,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
     // stages must start on a 1024-byte boundary (the swizzle follows address bits)
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
 
-    // the first copy must not wait on a cold descriptor fetch
-    if (threadIdx.x == 0) {
+    // the first copy must not wait on a cold descriptor fetch (SELF: no maps)
+    if (!SELF && threadIdx.x == 0) {
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_k)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_v)) : "memory");
     }
@@ -76,11 +81,13 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
         sm_hdr[0] = (ok && !stop) ? cnt : 0;
         sm_hdr[1] = (ok && !stop) ? h4 : 0;
         sm_hdr[2] = (ok && !stop) ? off : 0;
-        for (int s = 0; s < NS; ++s) {
-            mbar_init(&full[s], 2);  // the copies' arrive.expect_tx + the scales' arrive
-            mbar_init(&empty[s], static_cast<uint32_t>(Hkv));  // one consumer warp per kv head
+        if (!SELF) {
+            for (int s = 0; s < NS; ++s) {
+                mbar_init(&full[s], 2);  // the copies' arrive.expect_tx + the scales' arrive
+                mbar_init(&empty[s], static_cast<uint32_t>(Hkv));  // one consumer warp per kv head
+            }
+            fence_mbar_init();
         }
-        fence_mbar_init();
     }
     __syncthreads();
     const int nseg = sm_hdr[0];
@@ -97,7 +104,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
         // the first segment's pages (up to kPrewarmBytes of this CTA's) into L2;
         // the copies after the wait read them there (L2 is coherent with the
         // previous launch's writes, so a page it commits is read as written)
-        if (warp == NCW && nseg > 0) {
+        if (warp == (SELF ? 0 : NCW) && nseg > 0) {
             const int n0 = min(min(rec(0)[0].z, kPlanPids), static_cast<int>(kPrewarmBytes / (2 * p.page_bytes)));
             for (int j = lane; j < n0; j += 32) {
                 const int32_t pid = spids[j];
@@ -124,7 +131,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
     if (nseg == 0) return;
 
     // ======================= producer warp ========================================
-    if (warp == NCW) {
+    if (!SELF && warp == NCW) {
         const int32_t* bt = p.block_tables;
         auto npg_of = [&](int s) { return rec(s)[0].z; };
         auto advance = [&](int& s, int& j) {
@@ -236,10 +243,18 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
     uint32_t off[T::X4];
 #pragma unroll
     for (int x = 0; x < T::X4; ++x)
-        off[x] = static_cast<uint32_t>(h * T::TILE) +
+        off[x] = static_cast<uint32_t>((SELF ? 0 : h) * T::TILE) +
                  tile_chunk_off<KV4, HD>((lane & 7) + 8 * ((lane >> 3) & 1), 2 * x + (lane >> 4));
     const uint32_t st0 = smem_u32(stages);
     TmaHead<NT, MT> S;
+    // SELF: this warp's ring of RS slots ([K tile | V tile], sbytes each, and the
+    // page's two scales) and its page-id window (lane l: local tile mbase + l)
+    constexpr int RS = kSelfSlots<KV4, HD>;
+    uint8_t* ring = stages + static_cast<int64_t>(warp) * RS * sbytes;
+    float2* wmeta = meta + warp * RS;
+    const uint32_t ring0 = smem_u32(ring);
+    int mbase = 0;
+    int32_t mpid = 0;
     int kbase = 0;
     bool dead = false;
     int pend_s[2] = {-1, -1};
@@ -253,6 +268,49 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
         const int first = (wsub - kbase % WPH + WPH) % WPH;
         const int ntile = first < npg ? (npg - 1 - first) / WPH + 1 : 0;
         const bool has_tail = tail > 0 && wsub == (kbase + npg) % WPH;
+        // SELF: local tile i (segment page first + i * WPH) into slot i % RS, one
+        // copy group per call (empty past the warp's last tile)
+        auto refill = [&](int i0) {
+            const int i = i0 + lane;
+            int32_t v = 0;
+            if (i < ntile) {
+                const int pi = first + i * WPH;
+                v = (cidx == 0 && pi < kPlanPids)
+                        ? spids[pi]
+                        : __ldg(p.block_tables + static_cast<int64_t>(b) * p.max_blocks + r0.y + pi);
+                if (v < 0 || v >= p.num_pages) {
+                    flag(p.status, MG_DEV_BAD_PAGE_ID);
+                    v = 0;
+                }
+            }
+            mbase = i0;
+            mpid = v;
+        };
+        auto issue = [&](int i) {
+            if (i < ntile) {
+                if (i >= mbase + 32) refill(i);
+                const int32_t pid = __shfl_sync(0xffffffffu, mpid, i - mbase);
+                const int sl = i & (RS - 1);
+                uint8_t* dk = ring + static_cast<int64_t>(sl) * sbytes;
+                const int64_t go = static_cast<int64_t>(pid) * p.page_bytes + h * T::ROWB;
+                const int rs = Hkv * T::ROWB;
+#pragma unroll
+                for (int q = lane; q < 16 * T::CHUNKS; q += 32) {
+                    const int t = q / T::CHUNKS, j = q - t * T::CHUNKS;
+                    const uint32_t o = tile_chunk_off<KV4, HD>(t, j);
+                    cp_async16(dk + o, p.k_pool + go + t * rs + 16 * j);
+                    cp_async16(dk + T::TILE + o, p.v_pool + go + t * rs + 16 * j);
+                }
+                if (lane == 0) cp_async4(&wmeta[sl].x, p.k_scales + pid);
+                if (lane == 1) cp_async4(&wmeta[sl].y, p.v_scales + pid);
+            }
+            cp_async_commit();
+        };
+        if constexpr (SELF) {
+            mbase = -(1 << 30);
+#pragma unroll
+            for (int i = 0; i < RS; ++i) issue(i);
+        }
         if (ntile > 0 || has_tail) tma_load_q<KV4, HD, NT, SPLIT>(S, p, b, h, g, c);
         else tma_clear(S);
         if (has_tail && (lane & 15) < tail) {
@@ -270,7 +328,31 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
         };
         const uint32_t vdelta = static_cast<uint32_t>(sbytes / 2);
         int i = 0;
-        for (; PAIRS && i + 1 < ntile; i += 2) {
+        if constexpr (SELF) {
+            // two tiles a step: wait for their copy groups, run them, refill their slots
+            for (; i < ntile; i += 2) {
+                cp_async_wait_group<RS - 2>();
+                __syncwarp();
+                const int s0 = i & (RS - 1), s1 = (i + 1) & (RS - 1);
+                if (i + 1 < ntile) {
+                    const float2 m0 = wmeta[s0], m1 = wmeta[s1];
+                    const uint32_t kb[2] = {ring0 + static_cast<uint32_t>(s0 * sbytes),
+                                            ring0 + static_cast<uint32_t>(s1 * sbytes)};
+                    const float ksc[2] = {m0.x * p.sm_scale_log2, m1.x * p.sm_scale_log2}, vsc[2] = {m0.y, m1.y};
+                    uint64_t* const em[2] = {nullptr, nullptr};
+                    tma_page_tiles<KV4, HD, NT, SPLIT, 2, true>(S, kb, off, T::TILE, ksc, vsc, em, lane);
+                } else {
+                    const float2 m0 = wmeta[s0];
+                    const uint32_t kb[1] = {ring0 + static_cast<uint32_t>(s0 * sbytes)};
+                    const float ksc[1] = {m0.x * p.sm_scale_log2}, vsc[1] = {m0.y};
+                    uint64_t* const em[1] = {nullptr};
+                    tma_page_tiles<KV4, HD, NT, SPLIT, 1, PAIRS>(S, kb, off, T::TILE, ksc, vsc, em, lane);
+                }
+                issue(i + RS);
+                issue(i + RS + 1);
+            }
+        }
+        for (; !SELF && PAIRS && i + 1 < ntile; i += 2) {
             const int k0 = kbase + first + i * WPH, k1 = k0 + WPH;
             const int s0 = stage_of(k0), s1 = stage_of(k1);
             wait_full(k0);
@@ -281,7 +363,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
             uint64_t* const em[2] = {&empty[s0], &empty[s1]};
             tma_page_tiles<KV4, HD, NT, SPLIT, 2, true>(S, kb, off, vdelta, ksc, vsc, em, lane);
         }
-        for (; i < ntile; ++i) {
+        for (; !SELF && i < ntile; ++i) {
             const int k0 = kbase + first + i * WPH;
             const int s0 = stage_of(k0);
             wait_full(k0);
@@ -427,12 +509,16 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
         __threadfence();
         merge_partials<HD>(p, b, h, pbase, ncov, lane, wsub, WPH);
     }
+    if (SELF) cp_async_wait_all();  // (only empty groups are left) no copy outlives the CTA
 }
 
-template <bool KV4, int HD, int NT, bool SPLIT, int NW>
+template <bool KV4, int HD, int NT, bool SPLIT, int NW, bool SELF>
 mg_status launch_tma_one(const DecodeParams& p, const DecodePlan& pl, const CUtensorMap& tk, const CUtensorMap& tv,
                          cudaStream_t s) {
-    auto k = paged_decode_tma_kernel<KV4, HD, NT, SPLIT, NW>;
+    auto k = paged_decode_tma_kernel<KV4, HD, NT, SPLIT, NW, SELF>;
+    if (SELF && p.tma_ns != kSelfSlots<KV4, HD>)
+        return set_error(MG_ERR_UNSUPPORTED, "self-copying decode kernel: %d ring slots planned, %d compiled", p.tma_ns,
+                         kSelfSlots<KV4, HD>);
     if (pl.nconsumers > NW)
         return set_error(MG_ERR_UNSUPPORTED, "decode plan (%d consumer warps) does not fit the kernel (%d)",
                          pl.nconsumers, NW);
@@ -447,7 +533,7 @@ mg_status launch_tma_one(const DecodeParams& p, const DecodePlan& pl, const CUte
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(pl.grid);
-    cfg.blockDim = dim3(32 * (pl.nconsumers + 1));
+    cfg.blockDim = dim3(32 * (pl.nconsumers + (SELF ? 0 : 1)));
     cfg.dynamicSmemBytes = static_cast<size_t>(pl.smem_bytes);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
@@ -460,9 +546,9 @@ mg_status launch_tma_one(const DecodeParams& p, const DecodePlan& pl, const CUte
     return check_launch("paged_decode_tma_kernel");
 }
 
-template <bool KV4, int HD>
-mg_status launch_tma(const DecodeParams& p, const DecodePlan& pl, const CUtensorMap& tk, const CUtensorMap& tv,
-                     cudaStream_t s) {
+template <bool KV4, int HD, bool SELF>
+mg_status launch_tma_mode(const DecodeParams& p, const DecodePlan& pl, const CUtensorMap& tk, const CUtensorMap& tv,
+                          cudaStream_t s) {
     // 12 consumer warps + the producer (13 warps, budgeted as 16: 128 registers), or
     // 15 + 1 for 13-15 kv heads; 17 warps would be budgeted as 20 (96 registers)
     // (head_dim 128 with two n-tiles does not fit 128 registers: the register
@@ -470,19 +556,30 @@ mg_status launch_tma(const DecodeParams& p, const DecodePlan& pl, const CUtensor
     const bool w15 = pl.nconsumers > 12;
     if (pl.nt == 1) {
         if (pl.split_mode)
-            return w15 ? launch_tma_one<KV4, HD, 1, true, 15>(p, pl, tk, tv, s)
-                       : launch_tma_one<KV4, HD, 1, true, 12>(p, pl, tk, tv, s);
-        return w15 ? launch_tma_one<KV4, HD, 1, false, 15>(p, pl, tk, tv, s)
-                   : launch_tma_one<KV4, HD, 1, false, 12>(p, pl, tk, tv, s);
+            return w15 ? launch_tma_one<KV4, HD, 1, true, 15, SELF>(p, pl, tk, tv, s)
+                       : launch_tma_one<KV4, HD, 1, true, 12, SELF>(p, pl, tk, tv, s);
+        return w15 ? launch_tma_one<KV4, HD, 1, false, 15, SELF>(p, pl, tk, tv, s)
+                   : launch_tma_one<KV4, HD, 1, false, 12, SELF>(p, pl, tk, tv, s);
     }
     if constexpr (HD == 64) {
         if (pl.split_mode)
-            return w15 ? launch_tma_one<KV4, HD, 2, true, 15>(p, pl, tk, tv, s)
-                       : launch_tma_one<KV4, HD, 2, true, 12>(p, pl, tk, tv, s);
-        return w15 ? launch_tma_one<KV4, HD, 2, false, 15>(p, pl, tk, tv, s)
-                   : launch_tma_one<KV4, HD, 2, false, 12>(p, pl, tk, tv, s);
+            return w15 ? launch_tma_one<KV4, HD, 2, true, 15, SELF>(p, pl, tk, tv, s)
+                       : launch_tma_one<KV4, HD, 2, true, 12, SELF>(p, pl, tk, tv, s);
+        return w15 ? launch_tma_one<KV4, HD, 2, false, 15, SELF>(p, pl, tk, tv, s)
+                   : launch_tma_one<KV4, HD, 2, false, 12, SELF>(p, pl, tk, tv, s);
     }
     return set_error(MG_ERR_UNSUPPORTED, "bulk-copy decode kernel: head_dim 128 with a group over 4 (8) q heads");
+}
+
+// self_copy: the consumer warps copy their own tiles (INT4 pools only)
+template <bool KV4, int HD>
+mg_status launch_tma(const DecodeParams& p, const DecodePlan& pl, const CUtensorMap& tk, const CUtensorMap& tv,
+                     cudaStream_t s, bool self_copy) {
+    if constexpr (KV4) {
+        if (self_copy) return launch_tma_mode<KV4, HD, true>(p, pl, tk, tv, s);
+    }
+    if (self_copy) return set_error(MG_ERR_UNSUPPORTED, "self-copying decode kernel: INT4 pools only");
+    return launch_tma_mode<KV4, HD, false>(p, pl, tk, tv, s);
 }
 
 }  // namespace mg

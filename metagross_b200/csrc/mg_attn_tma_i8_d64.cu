@@ -3,5 +3,5 @@
 
 namespace mg {
 template mg_status launch_tma<false, 64>(const DecodeParams&, const DecodePlan&, const CUtensorMap&, const CUtensorMap&,
-                                       cudaStream_t);
+                                       cudaStream_t, bool);
 }  // namespace mg

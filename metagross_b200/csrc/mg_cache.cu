@@ -359,7 +359,36 @@ __global__ void __launch_bounds__(kAppendThreads, KEEP <= 2 ? 4 : 2) kv_append_k
         const int32_t page = j < p.max_blocks ? p.block_tables[static_cast<int64_t>(b) * p.max_blocks + j] : -1;
         uint8_t* pool = static_cast<uint8_t*>(kv ? p.v_pool : p.k_pool);
         float* scales = kv ? p.v_scales : p.k_scales;
-        if (page < 0 || page >= p.num_pages) {
+        const bool bad_page = page < 0 || page >= p.num_pages;
+        if (!p.scale_th && pe <= static_cast<int64_t>(kAppendThreads) * 8 * kKeep) {
+            // the whole page in registers (up to kKeep groups of 8 per thread): every
+            // load in flight at once, one pass over the staged and new rows; the
+            // loads do not wait for the page id (only the stores need it)
+            float v[kKeep][8];
+            float a = 0.0f;
+#pragma unroll
+            for (int u = 0; u < kKeep; ++u) {
+                const int64_t e = (static_cast<int64_t>(u) * kAppendThreads + threadIdx.x) * 8;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[u][i] = 0.0f;
+                if (e < pe) load8(e, v[u]);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) a = fmaxf(a, fabsf(v[u][i]));
+            }
+            a = block_max(a, red);
+            if (bad_page) {
+                if (threadIdx.x == 0) flag(p.status, MG_DEV_BAD_PAGE_ID);
+            } else {
+                const float sf = static_cast<float>(scale_from_absmax(a, INT4 ? 7.0 : 127.0));
+                if (threadIdx.x == 0) scales[page] = sf;
+                uint8_t* base = pool + static_cast<int64_t>(page) * (INT4 ? pe / 2 : pe);
+#pragma unroll
+                for (int u = 0; u < kKeep; ++u) {
+                    const int64_t e = (static_cast<int64_t>(u) * kAppendThreads + threadIdx.x) * 8;
+                    if (e < pe) store_codes<INT4>(base, e, v[u], sf);
+                }
+            }
+        } else if (bad_page) {
             if (threadIdx.x == 0) flag(p.status, MG_DEV_BAD_PAGE_ID);
         } else if (p.scale_th) {
             // one fresh scale per (token, head) D-vector, the reference's
@@ -393,29 +422,6 @@ __global__ void __launch_bounds__(kAppendThreads, KEEP <= 2 ? 4 : 2) kv_append_k
                         store_codes<INT4>(base, e, v[u], sf);
                     }
                 }
-            }
-        } else if (pe <= static_cast<int64_t>(kAppendThreads) * 8 * kKeep) {
-            // the whole page in registers (up to kKeep groups of 8 per thread): every
-            // load in flight at once, one pass over the staged and new rows
-            float v[kKeep][8];
-            float a = 0.0f;
-#pragma unroll
-            for (int u = 0; u < kKeep; ++u) {
-                const int64_t e = (static_cast<int64_t>(u) * kAppendThreads + threadIdx.x) * 8;
-#pragma unroll
-                for (int i = 0; i < 8; ++i) v[u][i] = 0.0f;
-                if (e < pe) load8(e, v[u]);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) a = fmaxf(a, fabsf(v[u][i]));
-            }
-            a = block_max(a, red);
-            const float sf = static_cast<float>(scale_from_absmax(a, INT4 ? 7.0 : 127.0));
-            if (threadIdx.x == 0) scales[page] = sf;
-            uint8_t* base = pool + static_cast<int64_t>(page) * (INT4 ? pe / 2 : pe);
-#pragma unroll
-            for (int u = 0; u < kKeep; ++u) {
-                const int64_t e = (static_cast<int64_t>(u) * kAppendThreads + threadIdx.x) * 8;
-                if (e < pe) store_codes<INT4>(base, e, v[u], sf);
             }
         } else {
             // larger pages: absmax pass, then a second pass that quantizes

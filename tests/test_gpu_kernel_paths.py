@@ -1,12 +1,14 @@
 """Both decode-attention kernels on the layouts either can serve.
 
 16-token pages with page scales and fp16 staged tails run the bulk-copy
-kernel for INT8 pools and the register-streaming kernel for INT4 pools by
-default (metagross_b200/csrc/mg_attention.cu, tma_applies); the environment
-variable METAGROSS_B200_ATTENTION forces one of them (``registers`` or
-``bulk``).  Each case here runs under both and is compared with the oracle's
-float64 dequantize-then-attend path (|out - ref| <= 2e-3 + 2^-11 |ref|), and
-the two kernels' outputs with each other.
+kernel: with its producer's bulk copies for INT8 pools, in its self-copying
+mode (consumer warps copy their own tiles) for INT4 pools
+(metagross_b200/csrc/mg_attention.cu, tma_mode).  The environment variable
+METAGROSS_B200_ATTENTION forces a path: ``registers`` (the
+register-streaming kernel), ``bulk`` (bulk copies for INT4 pools too);
+``self`` is the default behaviour.  Each case here runs under each and is compared
+with the oracle's float64 dequantize-then-attend path (|out - ref| <= 2e-3 +
+2^-11 |ref|), and the kernels' outputs with each other.
 """
 import numpy as np
 import pytest
@@ -58,7 +60,7 @@ def test_both_kernels_match_the_oracle_and_each_other(case, monkeypatch):
     cache, model, q = _build(kv, B, hq, hkv, lens, seed=sum(map(ord, case)))
     ref = model.attend(q.float().numpy(), 1.0 / 8)
     outs = {}
-    for path in ("registers", "bulk"):
+    for path in ("registers", "bulk", "self"):
         monkeypatch.setenv("METAGROSS_B200_ATTENTION", path)
         cache.invalidate_plan()
         out = cache.attend(0, q.cuda())
@@ -69,6 +71,7 @@ def test_both_kernels_match_the_oracle_and_each_other(case, monkeypatch):
         assert err < 2e-3, (path, err)
         outs[path] = o
     assert np.abs(outs["registers"] - outs["bulk"]).max() < 4e-3
+    assert np.abs(outs["registers"] - outs["self"]).max() < 4e-3
 
 
 def test_bulk_kernel_stream_k_int8():
@@ -91,7 +94,7 @@ def test_bulk_kernel_stream_k_int8():
 
 
 @pytest.mark.parametrize("case", ["int8_gqa8", "int4_gqa8", "int8_mha_tails"])
-@pytest.mark.parametrize("path", ["registers", "bulk"])
+@pytest.mark.parametrize("path", ["registers", "bulk", "self"])
 def test_settled_plan_launch_matches_the_plain_launch(case, path, monkeypatch):
     """MG_ATTN_PLAN_SETTLED moves the plan reads and an L2 warm-up of the first
     pages before the wait on the previous launch; the outputs are the plain
@@ -133,3 +136,26 @@ def test_settled_plan_launch_matches_the_plain_launch(case, path, monkeypatch):
                                       settled=False)
     torch.cuda.synchronize()
     assert torch.equal(out2, outs[-1])
+
+
+def test_self_copy_stream_k_int4(monkeypatch):
+    """The self-copying mode in stream-K (CTAs over several segments, page-id
+    windows refilled from the block table past the plan's first page ids),
+    INT4 32 q / 4 kv heads, with an empty and tail-only sequences."""
+    monkeypatch.setenv("METAGROSS_B200_ATTENTION", "self")
+    rng = np.random.default_rng(11)
+    B = 220
+    lens = np.maximum(1, np.exp(rng.normal(np.log(400), 1.0, B)).round().astype(int)).clip(max=4200).tolist()
+    lens[2] = 0
+    lens[9] = 7
+    lens[10] = 16 * 150 + 3
+    cache, model, q = _build("int4", B, 32, 4, lens, seed=12)
+    out = cache.attend(0, q.cuda())
+    torch.cuda.synchronize()
+    cache.check()
+    assert int(cache._plan.view(torch.int32)[5].item()) == 2  # stream-K
+    ref = model.attend(q.float().numpy(), 1.0 / 8)
+    o = out.float().cpu().numpy()
+    assert np.all(o[2] == 0.0)
+    err = float((np.abs(o - ref) - np.abs(ref) * 2.0 ** -11).max())
+    assert err < 2e-3, err
