@@ -284,6 +284,37 @@ def build(w, device, seed, ctx=None):
     return cache, Schedule(ctx, P), max_final, q, kn, vn, out
 
 
+def launch_floor_ms(w, device, reps=50):
+    """Average time of one attention launch, in a graph of the workload's L launches, when every sequence
+    holds a single staged token: the fixed per-launch cost (launch, plan records, q load, output write,
+    the launch boundary) that every launch of the workload pays on top of its page traffic."""
+    L = w["layers"]
+    ctx = torch.full((w["batch"],), 2, dtype=torch.int32)
+    cache, _, max_ctx, q, _, _, out = build(w, device, seed=7, ctx=ctx)
+    cache._decode_plan()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(g, stream=side):
+            for layer in range(L):
+                cache.attend(layer, q[layer], out=out[layer], max_context=max_ctx)
+    torch.cuda.current_stream().wait_stream(side)
+    for _ in range(3):
+        g.replay()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    cache.check()
+    del g
+    return e0.elapsed_time(e1) / (reps * L)
+
+
 def plan_steps(sched, n, device):
     """Precompute n steps of the schedule: device truncation args + host lengths after each step."""
     plans = []
@@ -704,6 +735,7 @@ def measure(w, name, steps, warmup, world, rank, local, device, e2e=True, equal_
     att_lens = timed_plans[-1][-1][2]
     att_bytes_per_launch = attention_bytes(att_lens, w)
     del g_att
+    floor_ms = launch_floor_ms(w, device)
     gather_ms = 0.0
     if world > 1:
         import torch.distributed as dist
@@ -725,6 +757,7 @@ def measure(w, name, steps, warmup, world, rank, local, device, e2e=True, equal_
 
     res = {"ms": ms, "steps": steps, "repeats": repeats, "ms_per_repeat": [round(x, 3) for x in ms_rep],
            "att_avg_ms": att_avg_ms, "att_bytes_per_launch": att_bytes_per_launch, "gather_ms": gather_ms,
+           "floor_ms": floor_ms,
            "clk": clk, "n_trunc": n_trunc, "L": L, "sharded": sharded, "loads": loads,
            "att_reps": att_reps, "cache": cache, "q": q}
 
@@ -926,6 +959,9 @@ def main():
                          "traffic": traffic_per_launch(args.workload),
                          "kernel": kernel, "algorithmic_bytes_per_launch": m["att_bytes_per_launch"],
                          "avg_launch_ms": m["att_avg_ms"],
+                         "launch_floor_ms": round(m["floor_ms"], 5),
+                         "floor_note": "the same graph of attention launches with one staged token per sequence: "
+                                       "the fixed cost each launch pays on top of its page traffic",
                          "timing": f"graph of the {L} attention launches (one per layer pool), CUDA events, "
                                    f"{m['att_reps']} replays"},
             "e2e": {"value": round(m["tot_e_bytes"] / (m["e_ms"] / 1e3) / 1e9, 1), "unit": "GB/s",

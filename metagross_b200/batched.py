@@ -148,13 +148,15 @@ class BatchedPagedKVCache:
             self.n_new.fill_(n)
             self._n_new_val = n
 
-    def append(self, layer: int, k_new: torch.Tensor, v_new: torch.Tensor) -> None:
-        """Write this step's tokens of one layer: k_new/v_new [B, T, Hkv, D] (fp16/fp32), n_new[b] <= T used."""
+    def append(self, layer: int, k_new: torch.Tensor, v_new: torch.Tensor, early_launch: bool = False) -> None:
+        """Write this step's tokens of one layer: k_new/v_new [B, T, Hkv, D] (fp16/fp32), n_new[b] <= T used.
+        early_launch: a programmatic dependent launch (MG_APPEND_EARLY_LAUNCH) -- for an append that follows
+        this library's own kernels (the previous layer's attention, the step plan), not a GEMM."""
         if k_new.dim() == 3:
             k_new, v_new = k_new.unsqueeze(1), v_new.unsqueeze(1)
         _get_C().kv_append(self.k_pool[layer], self.v_pool[layer], self.k_scales[layer], self.v_scales[layer],
                            self.staging_k[layer], self.staging_v[layer], self.block_tables, self.seq_lens,
-                           self.n_new, k_new, v_new, self.status)
+                           self.n_new, k_new, v_new, self.status, early_launch=early_launch)
         self._plan_last = False
 
     def append_rope(self, layer: int, qkv: torch.Tensor, num_q_heads: int, cos: torch.Tensor, sin: torch.Tensor,
@@ -332,7 +334,8 @@ class DecodeGraph:
         c = self.cache
         c.begin_step(self.n_new, plan=True)
         for layer in range(c.num_layers):
-            c.append(layer, self.k_new[layer], self.v_new[layer])
+            # every append follows one of the library's kernels (the plan step, the previous attention)
+            c.append(layer, self.k_new[layer], self.v_new[layer], early_launch=True)
             c.attend(layer, self.q[layer], scale=self.scale, out=self.out[layer],
                      max_context=c.max_blocks * c.page_size)
 

@@ -367,7 +367,8 @@ void free_sequences(torch::Tensor free_stack, torch::Tensor n_free, torch::Tenso
 
 void kv_append(torch::Tensor k_pool, torch::Tensor v_pool, torch::Tensor k_scales, torch::Tensor v_scales,
                torch::Tensor staging_k, torch::Tensor staging_v, torch::Tensor block_tables, torch::Tensor seq_lens,
-               torch::Tensor n_new, torch::Tensor k_new, torch::Tensor v_new, c10::optional<torch::Tensor> status) {
+               torch::Tensor n_new, torch::Tensor k_new, torch::Tensor v_new, c10::optional<torch::Tensor> status,
+               bool early_launch) {
     const c10::cuda::CUDAGuard guard(k_pool.device());
     auto p = make_pools(k_pool, v_pool, k_scales, v_scales, staging_k, staging_v, block_tables);
     const int64_t B = block_tables.size(0);
@@ -379,10 +380,10 @@ void kv_append(torch::Tensor k_pool, torch::Tensor v_pool, torch::Tensor k_scale
     TORCH_CHECK(k_new.size(0) == B && k_new.size(2) == p.L.num_kv_heads && k_new.size(3) == p.L.head_dim,
                 "k_new shape does not match the cache");
     auto kn = k_new.contiguous(), vn = v_new.contiguous();
-    check_status(mg_kv_append(&p.L, &p.ptrs, block_tables.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(),
-                              n_new.data_ptr<int32_t>(), static_cast<int32_t>(B), kn.data_ptr(), vn.data_ptr(),
-                              float_code(kn, "k_new"), static_cast<int32_t>(kn.size(1)), status_ptr(status),
-                              cur_stream()),
+    check_status(mg_kv_append_flags(&p.L, &p.ptrs, block_tables.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(),
+                                    n_new.data_ptr<int32_t>(), static_cast<int32_t>(B), kn.data_ptr(), vn.data_ptr(),
+                                    float_code(kn, "k_new"), static_cast<int32_t>(kn.size(1)),
+                                    early_launch ? MG_APPEND_EARLY_LAUNCH : 0u, status_ptr(status), cur_stream()),
                  "kv_append");
 }
 
@@ -668,7 +669,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           pybind11::arg("k_pool"), pybind11::arg("v_pool"), pybind11::arg("k_scales"), pybind11::arg("v_scales"),
           pybind11::arg("staging_k"), pybind11::arg("staging_v"), pybind11::arg("block_tables"),
           pybind11::arg("seq_lens"), pybind11::arg("n_new"), pybind11::arg("k_new"), pybind11::arg("v_new"),
-          pybind11::arg("status") = pybind11::none());
+          pybind11::arg("status") = pybind11::none(), pybind11::arg("early_launch") = false);
     m.def("decode_workspace_bytes", &decode_workspace_bytes, "Workspace bytes for paged_decode_attention");
     m.def("paged_decode_attention", &paged_decode_attention, "Fused batched paged decode attention",
           pybind11::arg("q"), pybind11::arg("k_pool"), pybind11::arg("v_pool"), pybind11::arg("k_scales"),

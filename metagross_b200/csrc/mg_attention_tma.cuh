@@ -108,6 +108,11 @@ __device__ __forceinline__ int tq_dim(int kk, int c, int s) {
 __device__ __forceinline__ uint32_t cvt8(uint32_t x) { return lop3_and_xor(x, 0x00FF00FFu, 0x64806480u); }  // 1152 + b
 __device__ __forceinline__ uint32_t lo4(uint32_t x) { return lop3_and_or(x, 0x000F000Fu, 0x64006400u); }  // 1032 + c
 __device__ __forceinline__ uint32_t hi4(uint32_t x) { return lop3_and_or(x, 0x00F000F0u, 0x64006400u); }  // 1152 + 16 c
+// The same for two's-complement nibbles s (c = s mod 16), the sign flip folded
+// into the one LOP3: (c ^ 8) = s + 8, so the low form is 1032 + s and the high
+// form 1152 + 16 s (the bits XORed in and ORed in do not overlap).
+__device__ __forceinline__ uint32_t lo4s(uint32_t x) { return lop3_and_xor(x, 0x000F000Fu, 0x64086408u); }
+__device__ __forceinline__ uint32_t hi4s(uint32_t x) { return lop3_and_xor(x, 0x00F000F0u, 0x64806480u); }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -397,7 +402,7 @@ __device__ __forceinline__ void tma_tile_scores(const TmaHead<NT, HD / 16>& S, u
             a[3] = cvt8(w8 >> 8);
         } else {
             const int j = kk >> 1;  // chunk
-            uint32_t w = kr[j >> 1][(j & 1) * 2] ^ 0x88888888u, w8 = kr[j >> 1][(j & 1) * 2 + 1] ^ 0x88888888u;
+            uint32_t w = kr[j >> 1][(j & 1) * 2], w8 = kr[j >> 1][(j & 1) * 2 + 1];
             if (kk & 1) {
                 w >>= 8;
                 w8 >>= 8;
@@ -407,10 +412,10 @@ __device__ __forceinline__ void tma_tile_scores(const TmaHead<NT, HD / 16>& S, u
             // rounding of a folded q . offsets term measurably reached the
             // output (2.03e-3 on the TinyLlama shape).  High nibbles stay 16 c
             // (q carries the 1/16).
-            a[0] = hsub2_u32(lo4(w), 0x64086408u);
-            a[1] = hsub2_u32(lo4(w8), 0x64086408u);
-            a[2] = hsub2_u32(hi4(w), 0x64806480u);
-            a[3] = hsub2_u32(hi4(w8), 0x64806480u);
+            a[0] = hsub2_u32(lo4s(w), 0x64086408u);
+            a[1] = hsub2_u32(lo4s(w8), 0x64086408u);
+            a[2] = hsub2_u32(hi4s(w), 0x64806480u);
+            a[3] = hsub2_u32(hi4s(w8), 0x64806480u);
         }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
@@ -444,13 +449,13 @@ __device__ __forceinline__ void tma_vfrag(const uint32_t (&vr)[TCfg<KV4, HD>::X4
         const int n = mt & 3;
         uint32_t x[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) x[i] = (r[i] ^ 0x88888888u) >> ((n >> 1) * 8);
+        for (int i = 0; i < 4; ++i) x[i] = r[i] >> ((n >> 1) * 8);
         const bool hi = n & 1;
         const uint32_t o = hi ? 0x64806480u : 0x64086408u;
-        a[0] = hsub2_u32(hi ? hi4(x[0]) : lo4(x[0]), o);
-        a[1] = hsub2_u32(hi ? hi4(x[2]) : lo4(x[2]), o);
-        a[2] = hsub2_u32(hi ? hi4(x[1]) : lo4(x[1]), o);
-        a[3] = hsub2_u32(hi ? hi4(x[3]) : lo4(x[3]), o);
+        a[0] = hsub2_u32(hi ? hi4s(x[0]) : lo4s(x[0]), o);
+        a[1] = hsub2_u32(hi ? hi4s(x[2]) : lo4s(x[2]), o);
+        a[2] = hsub2_u32(hi ? hi4s(x[1]) : lo4s(x[1]), o);
+        a[3] = hsub2_u32(hi ? hi4s(x[3]) : lo4s(x[3]), o);
     }
 }
 

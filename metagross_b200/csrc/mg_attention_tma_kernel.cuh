@@ -311,14 +311,15 @@ __global__ void __launch_bounds__((NW + (SELF ? 0 : 1)) * 32, 1)
 #pragma unroll
             for (int i = 0; i < RS; ++i) issue(i);
         }
-        if (ntile > 0 || has_tail) tma_load_q<KV4, HD, NT, SPLIT>(S, p, b, h, g, c);
-        else tma_clear(S);
+        // the tail rows' L1 prefetch goes out before q's loads, which the warp waits for
         if (has_tail && (lane & 15) < tail) {
             const __half* st16 = static_cast<const __half*>(lane < 16 ? p.staging_k : p.staging_v);
             const __half* rp = st16 + ((static_cast<int64_t>(b) * p.P + (lane & 15)) * Hkv + h) * HD;
 #pragma unroll
             for (int l = 0; l < HD * 2; l += 128) prefetch_l1(reinterpret_cast<const char*>(rp) + l);
         }
+        if (ntile > 0 || has_tail) tma_load_q<KV4, HD, NT, SPLIT>(S, p, b, h, g, c);
+        else tma_clear(S);
         // the warp's pages two at a time (one 32-token step), an odd last one alone
         auto wait_full = [&](int k) {
             if (!dead && !__all_sync(0xffffffffu, mbar_wait_limited(&full[stage_of(k)], round_of(k) & 1))) {

@@ -153,3 +153,15 @@ def test_planned_attention_rejects_unknown_flags_before_launch():
            ctypes.c_int64(1 << 20), ctypes.c_uint32(0x2), None, None)
     assert rc == 1
     assert b"unknown attention flags" in lib.mg_last_error()
+
+
+def test_append_rejects_unknown_flags_before_launch():
+    lib = ctypes.CDLL(LIB)
+    lib.mg_last_error.restype = ctypes.c_char_p
+    f = lib.mg_kv_append_flags
+    f.restype = ctypes.c_int
+    L = _Layout(0, 1, 16, 4, 64, 64, 1024)
+    p = ctypes.c_void_p(1 << 20)  # never dereferenced: refused before launch
+    rc = f(ctypes.byref(L), p, p, p, p, 1, p, p, 1, 1, ctypes.c_uint32(0x4), None, None)
+    assert rc == 1
+    assert b"unknown append flags" in lib.mg_last_error()
