@@ -426,7 +426,10 @@ __device__ __forceinline__ void tma_tile_scores(const TmaHead<NT, HD / 16>& S, u
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) sc[nt][i] = (CH2 ? sc[nt][i] + sc2[nt][i] : sc[nt][i]) - S.qb[nt][i & 1];
+        for (int i = 0; i < 4; ++i) {
+            sc[nt][i] = CH2 ? sc[nt][i] + sc2[nt][i] : sc[nt][i];
+            if (!KV4) sc[nt][i] -= S.qb[nt][i & 1];  // INT4 K codes come without offsets
+        }
 }
 
 // V^T A-fragment of m-tile mt from the ldmatrix.trans words vr of a page tile,
