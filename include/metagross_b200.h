@@ -318,8 +318,11 @@ MG_API mg_status mg_paged_decode_attention_planned(const mg_cache_layout* layout
  * dependent launch or waits for its own prerequisites before it releases its
  * dependents (every kernel of this library does; a plain launch does).  The
  * kernel then reads the plan and warms L2 with its first pages before it waits
- * for that launch to finish, on the SMs it has already left.  Never set it on
- * the launch right after mg_paged_decode_plan.  An unknown flag is
+ * for that launch to finish, on the SMs it has already left; with a plan from
+ * mg_plan_step, which records how many of each segment's pages were committed
+ * before the step, the bulk-copy kernel starts copying those pages (no launch
+ * of the step writes them) before the wait.  Never set it on the launch right
+ * after mg_paged_decode_plan or mg_plan_step.  An unknown flag is
  * MG_ERR_INVALID_ARGUMENT. */
 #define MG_ATTN_PLAN_SETTLED 0x1u
 MG_API mg_status mg_paged_decode_attention_planned_flags(const mg_cache_layout* layout, const mg_layer_ptrs* layer,

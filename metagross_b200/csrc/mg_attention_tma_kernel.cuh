@@ -100,11 +100,48 @@ __global__ void __launch_bounds__((NW + (SELF ? 0 : 1)) * 32, 1)
     }
     auto rec = [&](int k) -> const int4* { return k < kRecCache ? recs + 2 * k : flat + 2 * k; };
 
+    int pre = 0;  // producer: pages of the first segment copied before the wait
     if (settled) {
-        // the first segment's pages (up to kPrewarmBytes of this CTA's) into L2;
-        // the copies after the wait read them there (L2 is coherent with the
-        // previous launch's writes, so a page it commits is read as written)
-        if (warp == (SELF ? 0 : NCW) && nseg > 0) {
+        // The producer copies the first segment's pages that predate the step
+        // (the step plan's count, r1.w: no launch of this step writes them)
+        // before the wait, with their scales, into the first stages.
+        if (!SELF && warp == NCW && nseg > 0 && rec(0)[0].z > 0) {
+            const int G = p.tma_per_head ? 1 : 2;
+            int m = min(min(rec(0)[1].w, rec(0)[0].z), min(NS, 32));
+            if (G == 2) m &= ~1;
+            const int32_t pid = lane < m ? spids[lane] : 0;
+            if (m > 0 && !__any_sync(0xffffffffu, lane < m && (pid < 0 || pid >= p.num_pages))) {
+                const float ks = lane < m ? __ldg(p.k_scales + pid) : 0.0f;
+                const float vs = lane < m ? __ldg(p.v_scales + pid) : 0.0f;
+                const uint32_t tx = static_cast<uint32_t>(2 * p.page_bytes);
+                for (int i = 0; i < m; i += G) {
+                    if (G == 1) {  // stage i < NS: fresh, nothing to wait for
+                        const int32_t pi = __shfl_sync(0xffffffffu, pid, i);
+                        uint8_t* dk = stages + static_cast<int64_t>(i) * sbytes;
+                        if (lane == 0) mbar_arrive_expect_tx(&full[i], tx);
+                        __syncwarp();
+                        tma_page(dk, &tm_k, pi, &full[i], 1, Hkv, p.P, T::TILE, lane);
+                        tma_page(dk + sbytes / 2, &tm_v, pi, &full[i], 1, Hkv, p.P, T::TILE, lane);
+                    } else {
+                        const int j = lane >> 1;
+                        const int32_t pj = __shfl_sync(0xffffffffu, pid, min(i + j, 31));
+                        uint8_t* dst = stages + static_cast<int64_t>(i + j) * sbytes + ((lane & 1) ? sbytes / 2 : 0);
+                        if (j < 2 && (lane & 1) == 0) mbar_arrive_expect_tx(&full[i + j], tx);
+                        __syncwarp();
+                        if (j < 2) tma_page(dst, (lane & 1) ? &tm_v : &tm_k, pj, &full[i + j], 0, Hkv, p.P, T::TILE, 0);
+                    }
+                }
+                if (lane < m) {
+                    meta[lane] = make_float2(ks, vs);
+                    mbar_arrive(&full[lane]);
+                }
+                pre = m;
+            }
+        }
+        // otherwise the first segment's pages (up to kPrewarmBytes of this CTA's)
+        // into L2; the copies after the wait read them there (L2 is coherent with
+        // the previous launch's writes, so a page it commits is read as written)
+        if (pre == 0 && warp == (SELF ? 0 : NCW) && nseg > 0) {
             const int n0 = min(min(rec(0)[0].z, kPlanPids), static_cast<int>(kPrewarmBytes / (2 * p.page_bytes)));
             for (int j = lane; j < n0; j += 32) {
                 const int32_t pid = spids[j];
@@ -157,7 +194,7 @@ __global__ void __launch_bounds__((NW + (SELF ? 0 : 1)) * 32, 1)
         if (ns < nseg) advance(ns, nj);
         int32_t pid = raw_pid(cs, cj);
         int32_t pid_next = raw_pid(ns, nj);  // the next chunk's entries are in flight meanwhile
-        int k = 0, issued = 0;
+        int k = 0, issued = pre;  // pages [0, pre) of segment 0 went out before the wait
         bool dead = false;
         const uint32_t tx = static_cast<uint32_t>(2 * p.page_bytes);
         while (cs < nseg) {
@@ -176,8 +213,9 @@ __global__ void __launch_bounds__((NW + (SELF ? 0 : 1)) * 32, 1)
             // so far are published (their consumers may be what frees the stage).
             // With per-head copies, one page at a time.
             const int G = p.tma_per_head ? 1 : 2;
-            int pub = 0;  // pages [pub, issued - k) of the chunk are issued, scales not yet published
-            for (int i = 0; i < n; i += G) {
+            const int i0 = k == 0 ? pre : 0;  // (the pages copied before the wait are published too)
+            int pub = i0;  // pages [pub, issued - k) of the chunk are issued, scales not yet published
+            for (int i = i0; i < n; i += G) {
                 const int gi = min(G, n - i);
                 if (k + i + gi > NS) {
                     if (lane >= pub && k + lane < issued) {

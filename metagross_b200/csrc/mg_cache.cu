@@ -236,6 +236,7 @@ struct AppendParams {
     const __half* q_src;  // q heads of the new tokens, row stride new_stride
     __half* q_out;        // [batch, max_new, Hq, D] rotated q
     int32_t release_early;  // MG_APPEND_EARLY_LAUNCH: release the next launch at the start
+    FastDiv rowdiv;         // division by row (element offsets within a page are below 2^20)
 };
 
 // Rotate-half rotary embedding of one element pair at position pos (fp32
@@ -250,23 +251,24 @@ __device__ __forceinline__ float rope_elem(float own, float partner, float c, fl
 
 // Code of 8 consecutive elements into the pool at element e of a page (INT8:
 // 8 bytes, INT4: 4 bytes of nibbles, the even element in the low nibble),
-// through quant_code_fast (the same codes as the IEEE quotient x / sf).
+// through quant_codes8 (the same codes as the IEEE quotient x / sf).
 template <bool INT4>
 __device__ __forceinline__ void store_codes(uint8_t* page_base, int64_t e, const float (&v)[8], float sf) {
     const float inv = 1.0f / sf;
+    int q[8];
+    quant_codes8(v, sf, inv, INT4 ? 7.0f : 127.0f, q);
     if (!INT4) {
         uint32_t w0 = 0, w1 = 0;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            w0 |= (static_cast<uint32_t>(quant_code_fast(v[i], sf, inv, 127.0f)) & 0xFFu) << (8 * i);
-            w1 |= (static_cast<uint32_t>(quant_code_fast(v[4 + i], sf, inv, 127.0f)) & 0xFFu) << (8 * i);
+            w0 |= (static_cast<uint32_t>(q[i]) & 0xFFu) << (8 * i);
+            w1 |= (static_cast<uint32_t>(q[4 + i]) & 0xFFu) << (8 * i);
         }
         *reinterpret_cast<uint2*>(page_base + e) = make_uint2(w0, w1);
     } else {
         uint32_t w = 0;
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-            w |= (static_cast<uint32_t>(quant_code_fast(v[i], sf, inv, 7.0f)) & 0xFu) << (4 * i);
+        for (int i = 0; i < 8; ++i) w |= (static_cast<uint32_t>(q[i]) & 0xFu) << (4 * i);
         *reinterpret_cast<uint32_t*>(page_base + e / 2) = w;
     }
 }
@@ -337,7 +339,7 @@ __global__ void __launch_bounds__(kAppendThreads, KEEP <= 2 ? 4 : 2) kv_append_k
         Vec8<NT>::load(src + c, v);
         if (p.rope_cos != nullptr && kv == 0) {
             const int half = p.D / 2;
-            const int d = static_cast<int>(c - (c / p.D) * p.D);
+            const int d = static_cast<int>(c) % p.D;
             const bool lower = d < half;
             float w[8];
             Vec8<NT>::load(src + c + (lower ? half : -half), w);
@@ -353,9 +355,9 @@ __global__ void __launch_bounds__(kAppendThreads, KEEP <= 2 ? 4 : 2) kv_append_k
     };
     // 8 consecutive elements at element e of page j: staged rows, then this step's tokens
     auto load8 = [&](int64_t e, float (&v)[8]) {
-        const int t = static_cast<int>(e / row);
+        const int t = static_cast<int>(p.rowdiv.div(static_cast<uint32_t>(e)));
         const int tok = page_start + t;
-        const int64_t c = e - static_cast<int64_t>(t) * row;
+        const int64_t c = static_cast<int>(e) - t * row;
         if (tok < old) Vec8<ST>::load(staging + static_cast<int64_t>(t) * row + c, v);
         else load_new8(tok - old, c, v);
     };
@@ -665,7 +667,10 @@ mg_status append_launch(const mg_cache_layout* L, const mg_layer_ptrs* lp, const
     p.seq_lens = seq_lens;
     p.n_new = n_new;
     p.P = L->page_size;
+    // element offsets within a page (< 64 * row) divide exactly by the FastDiv of row while row <= 8192
+    MG_REQUIRE(row <= 8192, "num_kv_heads * head_dim must be at most 8192 for the append, got %lld", (long long)row);
     p.row = static_cast<int32_t>(row);
+    p.rowdiv = FastDiv(static_cast<uint32_t>(row));
     p.D = L->head_dim;
     p.scale_th = L->scale_layout == MG_SCALE_TOKEN_HEAD;
     p.num_pages = L->num_pages;

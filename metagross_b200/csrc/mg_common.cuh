@@ -43,19 +43,33 @@ __device__ __forceinline__ int quant_code(float x, float s, float qmax) {
     return static_cast<int>(roundf(k));
 }
 
-// quant_code(x, s, qmax) with the quotient formed as x * inv, inv = 1 / s
+// quant_code of 8 values with the quotients formed as x * inv, inv = 1 / s
 // rounded once.  x * inv is within 2^-23 |x / s| (plus its own rounding) of
 // the correctly rounded x / s, so the two round to the same integer unless the
-// quotient lies within a few ulps of a half-integer; only then is the IEEE
-// quotient taken.  Equal to quant_code for every input (NaN, infinities and the
-// clamp included): |x / s| <= qmax + 1 ulp whenever s = absmax / qmax covers x,
-// and a clamped quotient stays clamped.
-__device__ __forceinline__ int quant_code_fast(float x, float s, float inv, float qmax) {
-    if (isnan(x)) return 0;
-    const float q = x * inv;
-    const float f = fabsf(q - truncf(q));  // fractional part of |q|
-    if (fabsf(f - 0.5f) <= fabsf(q) * 4.8e-7f) return quant_code(x, s, qmax);
-    return static_cast<int>(roundf(fminf(qmax, fmaxf(-qmax, q))));
+// quotient lies within a few ulps of a half-integer: one test for the group,
+// and the IEEE quotient for all 8 only when one of them lies near a
+// half-integer or is not finite (the test is false for NaN quotients, and an
+// infinite x gives a NaN fractional part).  Away from half-integers round-to-
+// nearest-even and round-half-away agree, so the fast codes are one
+// conversion each.  The clamp commutes: |x / s| <= qmax + 1 ulp whenever
+// s = absmax / qmax covers x, and a clamped quotient stays clamped.  Codes
+// equal quant_code's for every input.
+__device__ __forceinline__ void quant_codes8(const float (&v)[8], float s, float inv, float qmax, int (&out)[8]) {
+    float q[8];
+    bool slow = false;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        q[i] = v[i] * inv;
+        const float f = fabsf(q[i] - truncf(q[i]));
+        slow |= !(fabsf(f - 0.5f) > fabsf(q[i]) * 4.8e-7f);
+    }
+    if (slow) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) out[i] = quant_code(v[i], s, qmax);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) out[i] = __float2int_rn(fminf(qmax, fmaxf(-qmax, q[i])));
+    }
 }
 
 // scale = absmax / qmax in double (csrc/quantize.cu:108-109), 1e-8 when the

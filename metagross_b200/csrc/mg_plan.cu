@@ -45,6 +45,7 @@ struct PlanParams {
     PlanLayout lay;
     int32_t* plan;
     int32_t* status;
+    const int32_t* n_new;  // the step's token counts (step plan), or null: no page is known to predate the step
 };
 
 __device__ __forceinline__ int block_sum(int v, int* scratch) {
@@ -84,9 +85,19 @@ __device__ __forceinline__ int block_scan_array(const int* vals, int* out, int n
 
 // Record k of CTA cta, whose records start at flat index off: into the flat
 // array, and into the CTA's inline area when k < kPlanInline.
+// r1.w: how many of the segment's pages (from lo) were committed before the
+// step (the step plan knows each sequence's n_new; 0 otherwise) -- pages no
+// append of the step writes, which a settled attention launch may copy before
+// its wait on the previous launch.
 __device__ __forceinline__ void write_rec(const PlanParams& pp, int cta, int off, int k, int b, int lo, int npg,
-                                          int tail, int pslot, int pbase, int ncov) {
-    const int4 r0 = make_int4(b, lo, npg, tail), r1 = make_int4(pslot, pbase, ncov, 0);
+                                          int tail, int pslot, int pbase, int ncov, int len_b) {
+    int old_pages = 0;
+    if (pp.n_new != nullptr) {
+        const int add = pp.n_new[b];
+        old_pages = add >= 0 && add <= len_b ? (len_b - add) / pp.P - lo : 0;
+        old_pages = old_pages < 0 ? 0 : (old_pages > npg ? npg : old_pages);
+    }
+    const int4 r0 = make_int4(b, lo, npg, tail), r1 = make_int4(pslot, pbase, ncov, old_pages);
     int4* f = reinterpret_cast<int4*>(pp.plan + pp.lay.off_flat + static_cast<int64_t>(off + k) * 8);
     f[0] = r0;
     f[1] = r1;
@@ -183,7 +194,7 @@ __device__ __forceinline__ void decode_plan_body(const PlanParams& pp) {
                 const int npg = max(0, min(uhi, np) - ulo);
                 const int tail = (uhi == u && tb > 0) ? tb : 0;
                 const int cta = aux[b] + j;
-                write_rec(pp, cta, cta, 0, b, ulo, npg, tail, k > 1 ? aux2[b] + j : -1, aux2[b], k);
+                write_rec(pp, cta, cta, 0, b, ulo, npg, tail, k > 1 ? aux2[b] + j : -1, aux2[b], k, len[b]);
                 first[3 * cta] = b;
                 first[3 * cta + 1] = ulo;
                 first[3 * cta + 2] = npg;
@@ -248,7 +259,8 @@ __device__ __forceinline__ void decode_plan_body(const PlanParams& pp) {
                 const int tail = (hi == ue - ub && tb > 0) ? tb : 0;
                 const bool whole = lo == 0 && hi == ue - ub;
                 const int first = cta_of_unit(ub);
-                write_rec(pp, c, offs[c], k, b, lo, npg, tail, whole ? -1 : aux2[b] + (c - first), aux2[b], aux[b]);
+                write_rec(pp, c, offs[c], k, b, lo, npg, tail, whole ? -1 : aux2[b] + (c - first), aux2[b], aux[b],
+                          len[b]);
                 if (k == 0) {
                     firstseg[3 * c] = b;
                     firstseg[3 * c + 1] = lo;
@@ -352,6 +364,7 @@ mg_status launch_decode_plan(const int32_t* block_tables, const int32_t* seq_len
     pp.lay = lay;
     pp.plan = plan;
     pp.status = status;
+    pp.n_new = alloc ? alloc->n_new : nullptr;
     const size_t tmp_ints = static_cast<size_t>(batch > 2 * G + 1 ? batch : 2 * G + 1);
     const size_t smem = (static_cast<size_t>(5) * batch + 3 + tmp_ints + 3 * static_cast<size_t>(G)) * sizeof(int);
     // the dynamic shared-memory opt-in, per kernel and device (raised as batches grow)

@@ -354,11 +354,23 @@ def test_append_rounds_half_integer_quotients_like_the_reference(kv):
     assert all(model.k_scales[int(model.block_tables[b, 0])] == 1.0 for b in range(B))
 
 
+def _record_words(B, G):
+    """Indices of the segment records' last word (r1.w) in a plan of batch B on G CTAs (plan_layout)."""
+    off_offs = 16 + G
+    off_recs = (off_offs + G + 7) // 8 * 8
+    off_pids = off_recs + G * 4 * 8
+    off_flat = off_pids + G * 128
+    off_empty = off_flat + (B + G) * 8
+    return list(range(off_recs + 7, off_pids, 8)) + list(range(off_flat + 7, off_empty, 8))
+
+
 @pytest.mark.parametrize("case", ["grow", "out_of_pages", "prefill"])
 def test_plan_step_equals_plan_append_then_plan(case):
     """mg_plan_step (allocation + decode plan in one launch) leaves the same
-    lengths, block tables, free stack, status and plan bytes as mg_plan_append
-    followed by mg_paged_decode_plan."""
+    lengths, block tables, free stack, status and plan words as mg_plan_append
+    followed by mg_paged_decode_plan -- except each segment record's count of
+    pages that predate the step (r1.w), which only the step plan knows:
+    clamp((new length - n_new) // P - lo, 0, npg)."""
     B, H, D, P = 40, 4, 64, 16
     g = np.random.default_rng(3)
     caches = [_cache_cls()(1, B, H, D, page_size=P, num_pages=B * 70 if case != "out_of_pages" else 300,
@@ -371,6 +383,8 @@ def test_plan_step_equals_plan_append_then_plan(case):
     steps = [torch.tensor(g.integers(0, 40, B), dtype=torch.int32)] if case != "grow" else [1] * 20
     if case == "out_of_pages":
         steps = [torch.full((B,), 200, dtype=torch.int32)]
+    G = torch.cuda.get_device_properties(0).multi_processor_count
+    wi = _record_words(B, G)
     for n in steps:
         a, b = caches
         a.begin_step(n)
@@ -381,7 +395,23 @@ def test_plan_step_equals_plan_append_then_plan(case):
         assert torch.equal(a.block_tables, b.block_tables)
         assert torch.equal(a.status, b.status)
         assert a.allocator.free_list() == b.allocator.free_list()
-        assert torch.equal(a._plan, b._plan)
+        wa = a._plan.view(torch.int32).cpu().numpy().copy()
+        wb = b._plan.view(torch.int32).cpu().numpy().copy()
+        assert np.all(wa[wi] == 0)
+        nn = np.full(B, n) if isinstance(n, int) else n.numpy()
+        lens_now = b.seq_lens.cpu().numpy()
+        for w in wi:
+            rec = wb[w - 7:w + 1]
+            bb, lo, npg = int(rec[0]), int(rec[1]), int(rec[2])
+            if npg == 0 and rec[3] == 0 and wb[w] == 0:
+                continue  # unused or tail-only record
+            # (after a refused step the lengths did not grow, and the count only comes out lower: still safe)
+            add = int(nn[bb])
+            old = lens_now[bb] - add if 0 <= add <= lens_now[bb] else -1
+            expect = min(max(old // P - lo, 0), npg) if old >= 0 else 0
+            assert wb[w] == expect, (w, rec)
+        wb[wi] = 0
+        assert np.array_equal(wa, wb)
     if case == "out_of_pages":
         assert int(caches[1].status.item()) & 0x1  # MG_DEV_OUT_OF_PAGES, nothing grew
         assert torch.equal(caches[1].seq_lens, lens.cuda())

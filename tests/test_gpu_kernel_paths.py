@@ -96,9 +96,10 @@ def test_bulk_kernel_stream_k_int8():
 @pytest.mark.parametrize("case", ["int8_gqa8", "int4_gqa8", "int8_mha_tails"])
 @pytest.mark.parametrize("path", ["registers", "bulk", "self"])
 def test_settled_plan_launch_matches_the_plain_launch(case, path, monkeypatch):
-    """MG_ATTN_PLAN_SETTLED moves the plan reads and an L2 warm-up of the first
-    pages before the wait on the previous launch; the outputs are the plain
-    launch's bit for bit, with an append (which commits pages) right before."""
+    """MG_ATTN_PLAN_SETTLED moves the plan reads, and the copies of the pages
+    that predate the step (or an L2 warm-up), before the wait on the previous
+    launch; the outputs are the plain launch's bit for bit, with an append
+    (which commits pages) right before."""
     from metagross_b200 import _C
 
     monkeypatch.setenv("METAGROSS_B200_ATTENTION", path)
@@ -107,8 +108,9 @@ def test_settled_plan_launch_matches_the_plain_launch(case, path, monkeypatch):
     g = torch.Generator().manual_seed(6)
     outs = []
     for settled in (False, True, False, True):
-        cache.begin_step(1)
-        cache.prepare_plan()
+        # the step plan: it records each segment's pages that predate the step, which a settled
+        # bulk-copy launch copies before its wait
+        cache.begin_step(1, plan=True)
         kn = torch.randn(B, hkv, 64, generator=g).half()
         vn = torch.randn(B, hkv, 64, generator=g).half()
         cache.append(0, kn.cuda(), vn.cuda())
