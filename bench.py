@@ -711,7 +711,9 @@ def measure(w, name, steps, warmup, world, rank, local, device, e2e=True, equal_
     cache.check()
 
     # ---- the attention kernel alone: a graph of the L attention launches ------------
-    cache._decode_plan()
+    # planned as the decode step plans (mg_plan_step, here with no new tokens), so that
+    # each launch, settled behind the previous one, copies its first pages before its wait
+    cache.begin_step(0, plan=True)
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())
     g_att = torch.cuda.CUDAGraph()
