@@ -291,62 +291,8 @@ __global__ void __launch_bounds__((NW + (SELF ? 0 : 1)) * 32, 1)
     uint8_t* ring = stages + static_cast<int64_t>(warp) * RS * sbytes;
     float2* wmeta = meta + warp * RS;
     const uint32_t ring0 = smem_u32(ring);
-    // SELF: the segment whose tiles the warp copies -- one segment ahead of the
-    // math from the end of a segment's tiles, so the next segment's first copies
-    // overlap this one's tail tile and merges -- and its page-id window
-    int is_cidx = -1, is_b = 0, is_lo = 0, is_first = 0, is_ntile = 0;
     int mbase = 0;
     int32_t mpid = 0;
-    auto refill = [&](int i0) {  // page ids of tiles i0 .. i0 + 31, one a lane
-        const int i = i0 + lane;
-        int32_t v = 0;
-        if (i < is_ntile) {
-            const int pi = is_first + i * WPH;
-            v = (is_cidx == 0 && pi < kPlanPids)
-                    ? spids[pi]
-                    : __ldg(p.block_tables + static_cast<int64_t>(is_b) * p.max_blocks + is_lo + pi);
-            if (v < 0 || v >= p.num_pages) {
-                flag(p.status, MG_DEV_BAD_PAGE_ID);
-                v = 0;
-            }
-        }
-        mbase = i0;
-        mpid = v;
-    };
-    // local tile i (segment page first + i * WPH) into slot i % RS, one copy
-    // group per call (empty past the segment's last tile of this warp)
-    auto issue = [&](int i) {
-        if (i < is_ntile) {
-            if (i >= mbase + 32) refill(i);
-            const int32_t pid = __shfl_sync(0xffffffffu, mpid, i - mbase);
-            const int sl = i & (RS - 1);
-            uint8_t* dk = ring + static_cast<int64_t>(sl) * sbytes;
-            const int64_t go = static_cast<int64_t>(pid) * p.page_bytes + h * T::ROWB;
-            const int rs = Hkv * T::ROWB;
-#pragma unroll
-            for (int q = lane; q < 16 * T::CHUNKS; q += 32) {
-                const int t = q / T::CHUNKS, j = q - t * T::CHUNKS;
-                const uint32_t o = tile_chunk_off<KV4, HD>(t, j);
-                cp_async16(dk + o, p.k_pool + go + t * rs + 16 * j);
-                cp_async16(dk + T::TILE + o, p.v_pool + go + t * rs + 16 * j);
-            }
-            if (lane == 0) cp_async4(&wmeta[sl].x, p.k_scales + pid);
-            if (lane == 1) cp_async4(&wmeta[sl].y, p.v_scales + pid);
-        }
-        cp_async_commit();
-    };
-    // begin copying segment cx, whose pages start at CTA page counter kb
-    auto start_issue = [&](int cx, int kb) {
-        const int4 q0 = rec(cx)[0];
-        is_cidx = cx;
-        is_b = q0.x;
-        is_lo = q0.y;
-        is_first = (wsub - kb % WPH + WPH) % WPH;
-        is_ntile = is_first < q0.z ? (q0.z - 1 - is_first) / WPH + 1 : 0;
-        mbase = -(1 << 30);
-#pragma unroll
-        for (int i = 0; i < RS; ++i) issue(i);
-    };
     int kbase = 0;
     bool dead = false;
     int pend_s[2] = {-1, -1};
@@ -360,8 +306,48 @@ __global__ void __launch_bounds__((NW + (SELF ? 0 : 1)) * 32, 1)
         const int first = (wsub - kbase % WPH + WPH) % WPH;
         const int ntile = first < npg ? (npg - 1 - first) / WPH + 1 : 0;
         const bool has_tail = tail > 0 && wsub == (kbase + npg) % WPH;
+        // SELF: local tile i (segment page first + i * WPH) into slot i % RS, one
+        // copy group per call (empty past the warp's last tile)
+        auto refill = [&](int i0) {
+            const int i = i0 + lane;
+            int32_t v = 0;
+            if (i < ntile) {
+                const int pi = first + i * WPH;
+                v = (cidx == 0 && pi < kPlanPids)
+                        ? spids[pi]
+                        : __ldg(p.block_tables + static_cast<int64_t>(b) * p.max_blocks + r0.y + pi);
+                if (v < 0 || v >= p.num_pages) {
+                    flag(p.status, MG_DEV_BAD_PAGE_ID);
+                    v = 0;
+                }
+            }
+            mbase = i0;
+            mpid = v;
+        };
+        auto issue = [&](int i) {
+            if (i < ntile) {
+                if (i >= mbase + 32) refill(i);
+                const int32_t pid = __shfl_sync(0xffffffffu, mpid, i - mbase);
+                const int sl = i & (RS - 1);
+                uint8_t* dk = ring + static_cast<int64_t>(sl) * sbytes;
+                const int64_t go = static_cast<int64_t>(pid) * p.page_bytes + h * T::ROWB;
+                const int rs = Hkv * T::ROWB;
+#pragma unroll
+                for (int q = lane; q < 16 * T::CHUNKS; q += 32) {
+                    const int t = q / T::CHUNKS, j = q - t * T::CHUNKS;
+                    const uint32_t o = tile_chunk_off<KV4, HD>(t, j);
+                    cp_async16(dk + o, p.k_pool + go + t * rs + 16 * j);
+                    cp_async16(dk + T::TILE + o, p.v_pool + go + t * rs + 16 * j);
+                }
+                if (lane == 0) cp_async4(&wmeta[sl].x, p.k_scales + pid);
+                if (lane == 1) cp_async4(&wmeta[sl].y, p.v_scales + pid);
+            }
+            cp_async_commit();
+        };
         if constexpr (SELF) {
-            if (is_cidx != cidx) start_issue(cidx, kbase);  // (not copied ahead at the last segment's end)
+            mbase = -(1 << 30);
+#pragma unroll
+            for (int i = 0; i < RS; ++i) issue(i);
         }
         // the tail rows' L1 prefetch goes out before q's loads, which the warp waits for
         if (has_tail && (lane & 15) < tail) {
@@ -404,8 +390,6 @@ __global__ void __launch_bounds__((NW + (SELF ? 0 : 1)) * 32, 1)
                 issue(i + RS);
                 issue(i + RS + 1);
             }
-            // every slot is free now: start the next segment's copies
-            if (cidx + 1 < nseg) start_issue(cidx + 1, kbase + npg);
         }
         for (; !SELF && PAIRS && i + 1 < ntile; i += 2) {
             const int k0 = kbase + first + i * WPH, k1 = k0 + WPH;
