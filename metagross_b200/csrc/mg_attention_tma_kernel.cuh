@@ -100,7 +100,9 @@ __global__ void __launch_bounds__((NW + (SELF ? 0 : 1)) * 32, 1)
     }
     auto rec = [&](int k) -> const int4* { return k < kRecCache ? recs + 2 * k : flat + 2 * k; };
 
-    int pre = 0;  // producer: pages of the first segment copied before the wait
+    // pages (producer) or tiles (SELF: each consumer warp's own) of the first
+    // segment copied before the wait
+    int pre = 0;
     if (settled) {
         // The producer copies the first segment's pages that predate the step
         // (the step plan's count, r1.w: no launch of this step writes them)
@@ -136,6 +138,37 @@ __global__ void __launch_bounds__((NW + (SELF ? 0 : 1)) * 32, 1)
                     mbar_arrive(&full[lane]);
                 }
                 pre = m;
+            }
+        }
+        // SELF: each consumer warp copies its own first tiles of the first
+        // segment's pages that predate the step into its ring's first slots
+        if (SELF && warp < NCW && nseg > 0) {
+            constexpr int RS0 = kSelfSlots<KV4, HD>;
+            const int wsub0 = WPH > 1 ? warp % WPH : 0, h0 = WPH > 1 ? warp / WPH : warp;
+            const int lim = min(rec(0)[1].w, rec(0)[0].z);  // pages [0, lim) of segment 0 predate the step
+            int n = lim > wsub0 ? (lim - 1 - wsub0) / WPH + 1 : 0;  // tile i: page wsub0 + i * WPH
+            n = min(n, RS0);
+            const int32_t pid = lane < n ? spids[wsub0 + lane * WPH] : 0;
+            if (n > 0 && !__any_sync(0xffffffffu, lane < n && (pid < 0 || pid >= p.num_pages))) {
+                uint8_t* ring0p = stages + static_cast<int64_t>(warp) * RS0 * sbytes;
+                float2* wmeta0 = meta + warp * RS0;
+                const int rs = Hkv * T::ROWB;
+                for (int i = 0; i < n; ++i) {
+                    const int32_t pi = __shfl_sync(0xffffffffu, pid, i);
+                    uint8_t* dk = ring0p + static_cast<int64_t>(i) * sbytes;
+                    const int64_t go = static_cast<int64_t>(pi) * p.page_bytes + h0 * T::ROWB;
+#pragma unroll
+                    for (int q = lane; q < 16 * T::CHUNKS; q += 32) {
+                        const int t = q / T::CHUNKS, j = q - t * T::CHUNKS;
+                        const uint32_t o = tile_chunk_off<KV4, HD>(t, j);
+                        cp_async16(dk + o, p.k_pool + go + t * rs + 16 * j);
+                        cp_async16(dk + T::TILE + o, p.v_pool + go + t * rs + 16 * j);
+                    }
+                    if (lane == 0) cp_async4(&wmeta0[i].x, p.k_scales + pi);
+                    if (lane == 1) cp_async4(&wmeta0[i].y, p.v_scales + pi);
+                    cp_async_commit();
+                }
+                pre = n;
             }
         }
         // otherwise the first segment's pages (up to kPrewarmBytes of this CTA's)
@@ -346,8 +379,7 @@ __global__ void __launch_bounds__((NW + (SELF ? 0 : 1)) * 32, 1)
         };
         if constexpr (SELF) {
             mbase = -(1 << 30);
-#pragma unroll
-            for (int i = 0; i < RS; ++i) issue(i);
+            for (int i = cidx == 0 ? pre : 0; i < RS; ++i) issue(i);
         }
         // the tail rows' L1 prefetch goes out before q's loads, which the warp waits for
         if (has_tail && (lane & 15) < tail) {
